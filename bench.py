@@ -1,0 +1,384 @@
+"""Benchmark of the int8 historical-KV decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg4]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1, one rank per GPU)
+
+Workload cfg1 (the one the headline metric is quoted
+on): per GPU 32 independent branches x 16 heads, head_dim 128, context 4096,
+one int8 K/V cache per layer for 24 layers (24 x 553.6 MB, each larger than
+L2).  One step = one decode token for every branch: for each of the 24 layer
+caches, a bf16 query per head -> fused int8 decode attention -> bf16 output.
+Weak scaling: every rank owns 32 branches (its shard of 32*N); no collective
+runs in the step; outputs are gathered to rank 0 over NCCL after timing.
+
+Prints one JSON line (rank 0).  `value` is the aggregate attention HBM
+throughput (algorithmic bytes / device time, max over ranks); `e2e` is the
+same metric through the public Python API with the queries copied from
+pinned host memory and the outputs read back every step.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: branches per GPU, heads, head_dim, context, layers, description
+    "cfg1": dict(branches=32, heads=16, d=128, ctx=4096, layers=24,
+                 desc="BASELINE config 1: 32 branches x 16 heads x d128, context 4096, 24 layer caches, bf16 q/out"),
+    "cfg4": dict(branches=8, heads=16, d=128, ctx=16384, layers=4,
+                 desc="BASELINE config 4 shape: 8 branches x 16 heads x d128, context 16384, 4 layer caches"),
+}
+
+
+def bytes_per_call(w) -> int:
+    rows = w["branches"] * w["heads"]
+    return rows * w["ctx"] * (2 * w["d"] + 8) + rows * w["d"] * 2 + rows * w["d"] * 2
+
+
+def load_peaks() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons with NVML during the timed region."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x1: "gpu_idle"}
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = getattr(torch.cuda.get_device_properties(device_index), "uuid", None)
+            h = None
+            if uuid is not None:
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + str(uuid)).encode())
+                except Exception:
+                    h = None
+            self.h = h or pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self.nv is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+def cpu_reference(w, steps: int, warmup: int, sample_branches: int, threads: int, budget_s: float) -> dict:
+    """The reference arithmetic restated on the CPU (oracle/), timed on a
+    bounded sample of the same workload: `sample_branches` branches of one
+    layer per step, all host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    rows = sample_branches * w["heads"]
+    g = np.random.Generator(np.random.PCG64(1))
+    k = g.integers(-127, 128, (rows, w["ctx"], w["d"]), dtype=np.int8).view(np.uint8)
+    v = g.integers(-127, 128, (rows, w["ctx"], w["d"]), dtype=np.int8).view(np.uint8)
+    ks = g.uniform(0.005, 0.03, (rows, w["ctx"])).astype(np.float32)
+    vs = g.uniform(0.005, 0.03, (rows, w["ctx"])).astype(np.float32)
+    q = oracle.bf16_round(g.standard_normal((rows, w["d"]), dtype=np.float32))
+    lens = np.full(sample_branches, w["ctx"], np.uint32)
+    per_call = rows * w["ctx"] * (2 * w["d"] + 8) + rows * w["d"] * 4
+    for _ in range(max(0, warmup)):
+        oracle.attention(q, k, v, ks, vs, lens, w["heads"], threads=threads)
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        oracle.attention(q, k, v, ks, vs, lens, w["heads"], threads=threads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    mean = sum(times) / len(times)
+    return {"value": per_call / mean / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_branches} branches x {w['heads']} heads x ctx {w['ctx']} x d{w['d']} of one layer "
+                      f"per step, {len(times)} timed steps, oracle/int8kv_oracle.c (reference arithmetic restated)"}
+
+
+def run_reference_arm(args, w) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    cb = cpu_reference(w, args.steps, args.warmup, sample_branches=1, threads=threads, budget_s=120.0)
+    n = args.gpus
+    line = {
+        "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+        "impl": "reference", "value": cb["value"], "unit": "GB/s", "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 KV, f32 accumulate", "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"],
+                   "heads": w["heads"], "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"],
+                   "parallelism": "replicas only (host cores)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference Candle CPU path cannot be built (no Rust toolchain); timed: its arithmetic restated in C",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
+    ap.add_argument("--layers", type=int, default=0, help="override the number of layer caches")
+    ap.add_argument("--split", type=int, default=0, help="fixed split size in tokens (0: automatic)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = dict(WORKLOADS[args.workload])
+    if args.layers:
+        w["layers"] = args.layers
+    if args.impl == "reference":
+        return run_reference_arm(args, w)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        pg = dist
+
+    pp = importlib.import_module("pop2-bezier_b200")
+    ops = pp.int8_kv_ops
+    N = pp._native
+
+    # ---- branch shard of this rank (independent branches, no collective)
+    total_branches = w["branches"] * world
+    shard_of, _ = pp.kv_cache.partition_branches([w["ctx"]] * total_branches, world)
+    mine = [b for b, s in enumerate(shard_of) if s == rank]
+    B, H, D, L, layers = len(mine), w["heads"], w["d"], w["ctx"], w["layers"]
+    rows = B * H
+
+    # ---- per-layer int8 caches, generated on the device as in config 0:
+    # K/V ~ N(0,1) f32, quantized per (token, head) by our quantizer.
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    caches = []
+    for _ in range(layers):
+        kv = []
+        for _ in range(2):
+            x = torch.randn(rows, L, D, device=dev, generator=gen)
+            kv.append(ops.quantize(x, check_finite=False))
+            del x
+        caches.append((kv[0][0], kv[1][0], kv[0][1], kv[1][1]))
+    lengths = torch.full((B,), L, dtype=torch.int32, device=dev)
+    qs = torch.randn(layers, rows, D, device=dev, generator=gen).to(torch.bfloat16)
+    outs = torch.empty(layers, rows, D, dtype=torch.bfloat16, device=dev)
+    arenas = [ops.arena_struct(k, v, ks, vs, H) for (k, v, ks, vs) in caches]
+    params = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+    params_ready = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
+                                   plan_ready=True)
+    ws = ops.new_workspace(arenas[0], params, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    lib = N.lib
+    lens_p, ws_p, st_p = C.c_void_p(lengths.data_ptr()), C.c_void_p(ws.data_ptr()), C.c_void_p(status.data_ptr())
+    q_ptrs = [C.c_void_p(qs[i].data_ptr()) for i in range(layers)]
+    o_ptrs = [C.c_void_p(outs[i].data_ptr()) for i in range(layers)]
+    arena_refs = [C.byref(a) for a in arenas]
+
+    def step(events=None):
+        # lengths are identical across layers in a step: plan once, reuse (DecodeMetadataCache)
+        N.check(lib.pp_b200_plan_ragged(arena_refs[0], C.byref(params), lens_p, 0, ws_p, ws.numel(), sp))
+        for i in range(layers):
+            if events is not None:
+                events[i][0].record(stream)
+            N.check(lib.pp_b200_decode_attention(arena_refs[i], C.byref(params_ready), q_ptrs[i], None, None, lens_p,
+                                                 o_ptrs[i], ws_p, ws.numel(), st_p, sp))
+            if events is not None:
+                events[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise SystemExit(f"device status after warm-up: {N.status_message(int(status.item()))}")
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    # ---- timed region: K steps, device time (CUDA events), max over ranks
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_total = start.elapsed_time(end)
+    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+
+    # ---- per-launch timing of the attention call (roofline), on the launching stream
+    n_ev = min(args.steps, 50)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
+           for _ in range(n_ev)]
+    for s in range(n_ev):
+        step(evs[s])
+    torch.cuda.synchronize()
+    call_ms = statistics.mean(e0.elapsed_time(e1) for per in evs for (e0, e1) in per)
+
+    per_call = bytes_per_call(dict(w, branches=B))
+    peak, peak_kind = load_peaks()
+    achieved = per_call / (call_ms * 1e-3) / 1e9
+    value = world * layers * per_call / (ms_step * 1e-3) / 1e9
+    tokens_per_s = total_branches / (ms_step * 1e-3)
+
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                traffic = json.load(f).get(args.workload)
+        except Exception:
+            traffic = None
+
+    # ---- end to end through the public API: host queries in, host outputs back
+    e2e = None
+    if not args.no_e2e:
+        q_host = qs.cpu().pin_memory()
+        o_host = torch.empty(outs.shape, dtype=outs.dtype).pin_memory()
+        q_dev = torch.empty_like(qs)
+        wsp = ws
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            ops_lens = lengths
+            for i, (k, v, ks, vs) in enumerate(caches):
+                ops.decode_attention(q_dev[i], k, v, ks, vs, ops_lens, H, out_dtype=torch.bfloat16,
+                                     split_tokens=args.split, workspace=wsp, out=outs[i])
+            o_host.copy_(outs, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        e_steps = max(1, min(args.steps, 50))
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([s0.elapsed_time(s1) / e_steps], dtype=torch.float64, device=dev)
+        if pg is not None:
+            pg.all_reduce(te, op=pg.ReduceOp.MAX)
+        e_ms = float(te.item())
+        e2e = {"value": world * layers * per_call / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
+               "d2h_bytes_per_step": o_host.numel() * o_host.element_size(), "ms_per_step": e_ms,
+               "tokens_per_s": total_branches / (e_ms * 1e-3)}
+
+    # ---- final gather of this step's outputs to rank 0 (NCCL, outside the timed region)
+    if pg is not None:
+        gathered = [torch.empty_like(outs) for _ in range(world)] if rank == 0 else None
+        pg.gather(outs, gathered, dst=0)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_reference(w, steps=3, warmup=1, sample_branches=1, threads=os.cpu_count() or 1, budget_s=20.0)
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 KV (bf16-rounded dequant), bf16 q/out, f32 accumulate", "data": "synthetic (seeded)",
+            "config": {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": B, "heads": H,
+                       "head_dim": D, "context": L, "layers": layers, "split_tokens": args.split,
+                       "parallelism": f"branch shards x{world} (no collective in the step)",
+                       "l2": "inputs larger than L2 (each layer cache > 126 MB), no flush"},
+            "tokens_per_s": tokens_per_s,
+            "percent_of_peak": 100.0 * value / (world * peak),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "per_launch_bytes": per_call, "per_launch_ms": call_ms,
+                         "timed": "pp_b200_decode_attention call (attention + combine kernels), CUDA events"},
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "gpu_launches": args.steps * (1 + 2 * layers),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

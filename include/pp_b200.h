@@ -1,0 +1,194 @@
+/*
+ * pp_b200.h -- C ABI of the B200 int8 historical-KV decode engine.
+ *
+ * This is the drop-in boundary for the reference's `int8_kv_ops` module
+ * (app/src/model/int8_kv_ops.rs), whose CUDA branches are Candle CustomOps
+ * launched through cudarc.  A Rust `extern "C"` crate binds these entry points
+ * in place of those CustomOps; INTEGRATION.md shows the binding.
+ *
+ * Conventions (style of app/native/aten_hip/cpp/painter_ffi.h:20-25):
+ *   - every entry point returns an int32 status:
+ *       PP_STATUS_OK (0)             success
+ *       PP_STATUS_PRECONDITION (1)   invalid geometry/argument: nothing was launched
+ *       PP_STATUS_INVALID_OUTPUT (2) a device check found invalid data (see pp_b200_read_status)
+ *       PP_STATUS_UNCERTAIN (3)      a CUDA launch/runtime error: device state uncertain,
+ *                                    the caller must discard the KV state (reload)
+ *   - pp_b200_last_error() returns a thread-local UTF-8 message for the last
+ *     non-OK status on the calling thread.  Messages carry the reference's
+ *     classifiable tokens (e.g. "CUDA_ERROR_OUT_OF_MEMORY", "EXECUTION_UNCERTAIN")
+ *     so app/src/inference.rs:34-92 keeps classifying them.
+ *   - all data pointers are caller-owned device memory; the library never
+ *     allocates device memory on the decode path (the workspace is supplied).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - all geometry is validated on the host before anything is launched.
+ *   - entry points are reentrant per stream; the only global state is a
+ *     per-device cache of device properties and kernel attributes.
+ */
+#ifndef PP_B200_H
+#define PP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PP_B200_ABI_VERSION 1u
+
+#define PP_STATUS_OK 0
+#define PP_STATUS_PRECONDITION 1
+#define PP_STATUS_INVALID_OUTPUT 2
+#define PP_STATUS_UNCERTAIN 3
+
+/* Element types of floating inputs/outputs. */
+#define PP_DTYPE_F32 0
+#define PP_DTYPE_BF16 1
+
+/* Bits a kernel may set in a caller-supplied device status word (uint32). */
+#define PP_DEV_NONFINITE_INPUT 0x1u  /* quantize saw a NaN/Inf (int8_kv_ops.rs:16) */
+#define PP_DEV_OFFSET_RANGE 0x2u     /* append offset >= capacity: row not written */
+#define PP_DEV_LENGTH_RANGE 0x4u     /* attention length > capacity: row output is NaN */
+#define PP_DEV_WAIT_TIMEOUT 0x8u     /* a bounded pipeline wait gave up: output undefined */
+
+/* Geometry of a caller-owned int8 KV arena for one layer, in the reference's
+ * batch-arena layout (app/src/model/cache.rs:301-478, int8_cache.rs:326-359):
+ *   k, v       u8  [rows, capacity, head_dim]   (signed int8 codes)
+ *   k_scale,
+ *   v_scale    f32 [rows, capacity]             (one scale per token and head)
+ * Row r = branch * heads + head.  k and v must be 16-byte aligned; scales
+ * need only 4-byte alignment (views at any row offset are accepted). */
+typedef struct PpKvArena {
+    uint32_t struct_size; /* sizeof(PpKvArena) */
+    uint32_t rows;        /* physical head rows = branches * heads */
+    uint32_t heads;       /* heads per branch (rows % heads == 0) */
+    uint32_t head_dim;    /* 64 or 128 */
+    uint32_t capacity;    /* token slots per row */
+    uint32_t reserved;
+    uint8_t* k;
+    uint8_t* v;
+    float* k_scale;
+    float* v_scale;
+} PpKvArena;
+
+/* Attention options. */
+typedef struct PpAttnParams {
+    uint32_t struct_size;   /* sizeof(PpAttnParams) */
+    uint32_t split_tokens;  /* 0: automatic stream-K balance over all SMs;
+                               else: fixed split size in tokens (the reference's
+                               split_tokens, int8_kv_ops.rs:52) */
+    int32_t q_dtype;        /* PP_DTYPE_F32 or PP_DTYPE_BF16, q is [rows, head_dim] */
+    int32_t out_dtype;      /* PP_DTYPE_F32 or PP_DTYPE_BF16, out is [rows, head_dim] */
+    float softmax_scale;    /* 0: 0.125 at head_dim 64 (int8_kv.cu:40), f32(1/sqrt(d)) otherwise */
+    uint32_t flags;         /* PP_ATTN_* */
+    uint32_t max_ctas;      /* 0: one CTA per SM */
+    uint32_t reserved;
+} PpAttnParams;
+
+/* The workspace already holds the plan made by pp_b200_plan_ragged for the
+ * same arena geometry, params and lengths (reuse across layers and queries,
+ * as DecodeMetadataCache does, app/src/model/decode_metadata.rs:39-142). */
+#define PP_ATTN_PLAN_READY 0x1u
+
+uint32_t pp_b200_abi_version(void);
+const char* pp_b200_last_error(void);
+
+/* Symmetric per-(token, head) int8 quantization of `rows` vectors of
+ * head_dim elements: replaces int8_kv_ops::quantize (int8_kv_ops.rs:11-29,
+ * kernels pp_i8_scale + pp_i8_pack, int8_kv.cu:8-18).
+ * x: f32/bf16 [rows, head_dim]; packed: u8 [rows, head_dim]; scales: f32 [rows].
+ * status (nullable, device uint32): PP_DEV_NONFINITE_INPUT is OR-ed in when
+ * an input element is not finite. */
+int32_t pp_b200_quantize(const void* x, int32_t x_dtype, uint64_t rows, uint32_t head_dim,
+                         uint8_t* packed, float* scales, uint32_t* status, void* stream);
+
+/* Dequantization: replaces int8_kv_ops::dequantize (int8_kv_ops.rs:30-40,
+ * kernel pp_i8_unpack int8_kv.cu:19-22).  out = (i8) packed * scale[row],
+ * rounded to bf16 first when round_bf16 != 0 (the `to_dtype(BF16)` of
+ * int8_cache.rs:368), written as out_dtype. */
+int32_t pp_b200_dequantize(const uint8_t* packed, const float* scales, uint64_t rows,
+                           uint32_t head_dim, int32_t round_bf16, int32_t out_dtype, void* out,
+                           void* stream);
+
+/* Quantize-and-append one new K/V token per row: replaces the commit branch of
+ * Int8LayerCache::encoded (int8_cache.rs:293-312) plus the arena writes of
+ * LayerCache::query_batch_with_plan (cache.rs:415-459, slice_set / scatter_set).
+ * k_new, v_new: f32/bf16 [rows, head_dim].  offsets: device u32 [rows/heads],
+ * the per-branch write slot (the past length).  commit=0 writes the partial
+ * query placeholder (zero codes, scale 1.0, int8_cache.rs:305-310) instead.
+ * status (nullable): PP_DEV_NONFINITE_INPUT, PP_DEV_OFFSET_RANGE. */
+int32_t pp_b200_quant_append(const PpKvArena* arena, const void* k_new, const void* v_new,
+                             int32_t dtype, const uint32_t* offsets, uint32_t commit,
+                             uint32_t* status, void* stream);
+
+/* Copies each row's committed prefix from one arena to another of larger
+ * capacity: the growth/COW copy of LayerCache::query (cache.rs:246-266) and the
+ * batch-row adoption copy (cache.rs:393-414).  lengths: device u32 [rows/heads]. */
+int32_t pp_b200_copy_prefix(const PpKvArena* src, const PpKvArena* dst, const uint32_t* lengths,
+                            void* stream);
+
+/* Workspace bytes pp_b200_decode_attention / pp_b200_plan_ragged need for this
+ * geometry (an upper bound independent of the device-resident lengths). */
+size_t pp_b200_attention_workspace_size(const PpKvArena* arena, const PpAttnParams* params);
+
+/* Ragged bookkeeping: turns device-resident per-branch lengths into the split
+ * work list the attention kernel consumes, inside `workspace`.  Restates the
+ * per-row geometry of BatchWritePlan / DecodeMetadataCache
+ * (write_plan.rs:48-93, decode_metadata.rs:107-125) as device tables.
+ * scratch_token != 0 selects the reference mode of pp_b200_decode_attention. */
+int32_t pp_b200_plan_ragged(const PpKvArena* arena, const PpAttnParams* params,
+                            const uint32_t* lengths, uint32_t scratch_token, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Fused int8 decode attention (dequant -> QK^T -> softmax -> PV, split-K with
+ * a log-sum-exp combine): replaces int8_kv_ops::attention (int8_kv_ops.rs:42-55,
+ * kernels pp_i8_attention + pp_i8_merge, int8_kv.cu:28-59).
+ *   q        [rows, head_dim] (params->q_dtype)
+ *   lengths  device u32 [rows/heads]
+ *   scratch_k, scratch_v: f32 [rows, head_dim] or both NULL.
+ *     non-NULL (reference mode): a row attends to lengths[b] int8 history
+ *       tokens plus the f32 scratch token; lengths[b] > capacity gives NaN.
+ *     NULL (history mode): a row attends to lengths[b] int8 tokens;
+ *       0 or > capacity gives NaN.
+ *   out      [rows, head_dim] (params->out_dtype)
+ * History values are dequantized exactly as pp_i8_load does: bf16(i8 * scale).
+ * status (nullable): PP_DEV_LENGTH_RANGE, PP_DEV_WAIT_TIMEOUT. */
+int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* params,
+                                 const void* q, const float* scratch_k, const float* scratch_v,
+                                 const uint32_t* lengths, void* out, void* workspace,
+                                 size_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Decodes device status bits into a message (static storage). */
+const char* pp_b200_status_message(uint32_t status_bits);
+
+/* Physical batch rows with the reference's overflow rules:
+ * checked_batch_rows (app/src/model/batch_geometry.rs:4-16). */
+int32_t pp_b200_checked_batch_rows(uint64_t logical_rows, uint32_t guidance,
+                                   uint64_t* physical_rows);
+
+/* Host-side write-plan validation: checked_shape (write_plan.rs:27-45) with
+ * the arena capacity in place of MAX_CONTEXT (offsets must leave a slot). */
+int32_t pp_b200_check_write_offsets(const uint64_t* past_lens, uint64_t count, uint32_t heads,
+                                    uint32_t head_dim, uint32_t capacity);
+
+/* Branch scheduler: deterministic longest-processing-time partition of
+ * independent branches across shards (GPUs).  cost[i] is branch i's KV work
+ * (its context length); shard_of_branch[i] receives its shard and
+ * shard_cost[s] the total per shard.  Branches are the independent lanes of
+ * NativeEngine::generate_parallel (app/src/inference/batch.rs:241-558), which
+ * the reference runs on one device. */
+int32_t pp_b200_sched_partition(const uint64_t* cost, uint32_t n_branches, uint32_t n_shards,
+                                uint32_t* shard_of_branch, uint64_t* shard_cost);
+
+/* On-device self-check run before int8 caches are created: replaces
+ * int8_kv_ops::prepare (int8_kv_ops.rs:57-103) and is called where
+ * PrimitiveModel::prepare_int8_kv calls it (int8_policy.rs:29-56).  Runs the
+ * reference's own fixtures (quantize round trip within 0.009, attention within
+ * 2e-5 of scalar host loops, offsets/splits {32,128}) on `device`. */
+int32_t pp_b200_prepare(int32_t device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PP_B200_H */

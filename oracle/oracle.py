@@ -1,0 +1,136 @@
+"""ctypes binding of the CPU oracle (oracle/int8kv_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline / reference arm of bench.py.  The product never imports this.
+Build the shared library with `make -C oracle`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle_int8kv.so")
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} missing: run `make -C oracle`")
+        L = C.CDLL(LIB_PATH)
+        vp, u32, u64, i32, f32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float
+        L.oracle_bf16_round.restype = f32
+        L.oracle_bf16_round.argtypes = [f32]
+        L.oracle_quantize_f32.restype = i32
+        L.oracle_quantize_f32.argtypes = [vp, u64, u32, vp, vp]
+        L.oracle_quantize_bf16.restype = i32
+        L.oracle_quantize_bf16.argtypes = [vp, u64, u32, vp, vp]
+        L.oracle_dequantize.restype = None
+        L.oracle_dequantize.argtypes = [vp, vp, u64, u32, vp, i32]
+        L.oracle_attention.restype = i32
+        L.oracle_attention.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, f32, vp, i32]
+        L.oracle_quant_append.restype = i32
+        L.oracle_quant_append.argtypes = [vp, vp, u32, u32, u32, u32, vp, i32, vp, vp, vp, vp]
+        L.oracle_max_threads.restype = i32
+        L.oracle_max_threads.argtypes = []
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data if a is not None else 0)
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """RNE f32 -> bf16 bits (half::bf16::from_f32 semantics for finite values)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFFFFFF
+    return (u >> 16).astype(np.uint16)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+class NonFiniteInput(ValueError):
+    pass
+
+
+def quantize(x: np.ndarray, head_dim: int | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """int8_kv_ops.rs:13-21 on rows of head_dim.  x: f32, or uint16 bf16 bits."""
+    d = head_dim or x.shape[-1]
+    rows = x.size // d
+    packed = np.empty(rows * d, dtype=np.uint8)
+    scales = np.empty(rows, dtype=np.float32)
+    if x.dtype == np.uint16:
+        xs = np.ascontiguousarray(x)
+        rc = lib().oracle_quantize_bf16(_p(xs), rows, d, _p(packed), _p(scales))
+    else:
+        xs = np.ascontiguousarray(x, dtype=np.float32)
+        rc = lib().oracle_quantize_f32(_p(xs), rows, d, _p(packed), _p(scales))
+    if rc == 1:
+        raise NonFiniteInput("non-finite INT8 KV input")
+    if rc:
+        raise ValueError(f"oracle quantize failed ({rc})")
+    return packed.reshape(x.shape[:-1] + (d,)), scales.reshape(x.shape[:-1])
+
+
+def dequantize(packed: np.ndarray, scales: np.ndarray, round_bf16: bool) -> np.ndarray:
+    d = packed.shape[-1]
+    rows = packed.size // d
+    out = np.empty(packed.size, dtype=np.float32)
+    pk = np.ascontiguousarray(packed, dtype=np.uint8)
+    sc = np.ascontiguousarray(scales, dtype=np.float32)
+    lib().oracle_dequantize(_p(pk), _p(sc), rows, d, _p(out), int(round_bf16))
+    return out.reshape(packed.shape)
+
+
+def attention(q, k, v, ks, vs, lengths, heads: int, *, sk=None, sv=None, scale: float | None = None,
+              threads: int = 1) -> np.ndarray:
+    """Batched int8 decode attention (reference arithmetic; see the C file).
+
+    q f32 [rows, d]; k, v u8 [rows, cap, d]; ks, vs f32 [rows, cap];
+    lengths u32 [rows/heads]; sk, sv f32 [rows, d] or None.  Returns f32 [rows, d].
+    """
+    rows, cap, d = k.shape
+    if scale is None:
+        scale = 0.125 if d == 64 else float(np.float32(1.0 / np.sqrt(d)))
+    args = [np.ascontiguousarray(q, dtype=np.float32).reshape(rows, d),
+            np.ascontiguousarray(k, dtype=np.uint8), np.ascontiguousarray(v, dtype=np.uint8),
+            np.ascontiguousarray(ks, dtype=np.float32), np.ascontiguousarray(vs, dtype=np.float32)]
+    skc = None if sk is None else np.ascontiguousarray(sk, dtype=np.float32).reshape(rows, d)
+    svc = None if sv is None else np.ascontiguousarray(sv, dtype=np.float32).reshape(rows, d)
+    lens = np.ascontiguousarray(lengths, dtype=np.uint32)
+    out = np.empty((rows, d), dtype=np.float32)
+    rc = lib().oracle_attention(_p(args[0]), _p(args[1]), _p(args[2]), _p(args[3]), _p(args[4]), _p(skc), _p(svc),
+                                _p(lens), rows, heads, d, cap, scale, _p(out), threads)
+    if rc:
+        raise ValueError(f"oracle attention failed ({rc})")
+    return out
+
+
+def quant_append(xk, xv, heads: int, offsets, commit: bool, k_arena, v_arena, ks_arena, vs_arena) -> None:
+    """In-place oracle append into numpy arenas [rows, cap, d] / [rows, cap]."""
+    rows, cap, d = k_arena.shape
+    xk = np.ascontiguousarray(xk, dtype=np.float32)
+    xv = np.ascontiguousarray(xv, dtype=np.float32)
+    offs = np.ascontiguousarray(offsets, dtype=np.uint32)
+    rc = lib().oracle_quant_append(_p(xk), _p(xv), rows, heads, d, cap, _p(offs), int(commit), _p(k_arena),
+                                   _p(v_arena), _p(ks_arena), _p(vs_arena))
+    if rc == 1:
+        raise NonFiniteInput("non-finite INT8 KV input")
+    if rc:
+        raise ValueError(f"oracle append failed ({rc})")
+
+
+def max_threads() -> int:
+    return int(lib().oracle_max_threads())

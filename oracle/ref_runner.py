@@ -1,0 +1,99 @@
+"""Runs the reference's own CUDA kernels (compiled from its sources into
+oracle/_ref/ by oracle/Makefile) on device tensors, with the launch geometry
+of the reference's CustomOps (app/src/model/int8_kv_ops.rs:120-161).
+
+TEST INFRASTRUCTURE ONLY: used to pin the oracle (tests/golden/make_golden.py)
+and by GPU parity tests that compare against the reference kernels directly.
+Nothing here reads the reference tree at run time; it needs only the cubins.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+INT8_CUBIN = os.path.join(HERE, "_ref", "int8_kv_ref.cubin")
+
+
+def available() -> bool:
+    return os.path.exists(INT8_CUBIN)
+
+
+class _Driver:
+    def __init__(self):
+        self.cu = C.CDLL("libcuda.so.1")
+        self.cu.cuModuleLoadData.argtypes = [C.POINTER(C.c_void_p), C.c_void_p]
+        self.cu.cuModuleGetFunction.argtypes = [C.POINTER(C.c_void_p), C.c_void_p, C.c_char_p]
+        self.cu.cuLaunchKernel.argtypes = [C.c_void_p, C.c_uint, C.c_uint, C.c_uint, C.c_uint, C.c_uint, C.c_uint,
+                                           C.c_uint, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
+        self.cu.cuFuncSetAttribute.argtypes = [C.c_void_p, C.c_int, C.c_int]
+
+    def check(self, rc: int, what: str) -> None:
+        if rc != 0:
+            raise RuntimeError(f"{what} failed: CUresult {rc}")
+
+
+class RefInt8Kernels:
+    """pp_i8_scale / pp_i8_pack / pp_i8_unpack / pp_i8_attention / pp_i8_merge."""
+
+    def __init__(self, cubin: str = INT8_CUBIN):
+        torch.cuda.init()
+        torch.empty(1, device="cuda")  # make the primary context current
+        self.d = _Driver()
+        with open(cubin, "rb") as f:
+            self._image = f.read()
+        self._buf = C.create_string_buffer(self._image, len(self._image))
+        self.mod = C.c_void_p()
+        self.d.check(self.d.cu.cuModuleLoadData(C.byref(self.mod), C.cast(self._buf, C.c_void_p)), "cuModuleLoadData")
+        self.fn = {}
+        for name in ("pp_i8_scale", "pp_i8_pack", "pp_i8_unpack", "pp_i8_attention", "pp_i8_merge"):
+            f = C.c_void_p()
+            self.d.check(self.d.cu.cuModuleGetFunction(C.byref(f), self.mod, name.encode()), name)
+            self.fn[name] = f
+
+    def _launch(self, name, grid, block, smem, args):
+        holders = []
+        for a in args:
+            if isinstance(a, torch.Tensor):
+                holders.append(C.c_void_p(a.data_ptr()))
+            else:
+                holders.append(a)
+        params = (C.c_void_p * len(holders))(*[C.cast(C.pointer(h), C.c_void_p) for h in holders])
+        stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        if smem > 48 * 1024:
+            self.d.check(self.d.cu.cuFuncSetAttribute(self.fn[name], 8, smem), "cuFuncSetAttribute")
+        self.d.check(self.d.cu.cuLaunchKernel(self.fn[name], grid[0], grid[1], 1, block, 1, 1, smem, stream, params,
+                                              None), name)
+
+    def quantize(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """x f32 [..., 64] contiguous -> (u8 codes, f32 scales [...])."""
+        assert x.dtype == torch.float32 and x.is_contiguous() and x.shape[-1] == 64
+        rows = x.numel() // 64
+        scale = torch.empty(rows, dtype=torch.float32, device=x.device)
+        packed = torch.empty(x.numel(), dtype=torch.uint8, device=x.device)
+        self._launch("pp_i8_scale", (rows, 1), 64, 0, [x, scale, C.c_uint64(rows)])
+        n = x.numel()
+        self._launch("pp_i8_pack", ((n + 255) // 256, 1), 256, 0, [x, scale, packed, C.c_uint64(n)])
+        return packed.reshape(x.shape), scale.reshape(x.shape[:-1])
+
+    def dequantize(self, packed: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+        n = packed.numel()
+        out = torch.empty(n, dtype=torch.float32, device=packed.device)
+        self._launch("pp_i8_unpack", ((n + 255) // 256, 1), 256, 0, [packed, scale, out, C.c_uint64(n)])
+        return out.reshape(packed.shape)
+
+    def attention(self, q, k, v, ks, vs, sk, sv, past, heads: int, split_tokens: int) -> torch.Tensor:
+        """Reference-mode attention exactly as cuda::Attention launches it."""
+        rows, cap, d = k.shape
+        assert d == 64 and cap <= 1024
+        split = 128 if split_tokens == 0 else max(32, min(1024, split_tokens))
+        splits = (cap + 1 + split - 1) // split
+        partial = torch.empty(rows * splits * 66, dtype=torch.float32, device=q.device)
+        out = torch.empty(rows * 64, dtype=torch.float32, device=q.device)
+        self._launch("pp_i8_attention", (rows, splits), 128, (split + 128) * 4,
+                     [q, k, v, ks, vs, sk, sv, past, partial, C.c_uint32(heads), C.c_uint32(cap), C.c_uint32(split),
+                      C.c_uint32(splits)])
+        self._launch("pp_i8_merge", (rows, 1), 64, 0, [partial, out, C.c_uint32(splits)])
+        return out.reshape(rows, 1, 64)

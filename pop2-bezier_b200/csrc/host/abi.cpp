@@ -1,0 +1,338 @@
+// C ABI implementation: host-side validation, TMA descriptor encoding and
+// kernel launches for the int8 historical-KV engine.
+//
+// Validation mirrors the reference's checks before any device work
+// (app/src/model/int8_kv_ops.rs:5-10 `geometry`, :44-48 attention `ensure!`s,
+// app/src/model/write_plan.rs:27-45 `checked_shape`).  Nothing is launched
+// when a check fails (status PP_STATUS_PRECONDITION).
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+
+namespace pp {
+uint32_t attention_scale_box_elems();
+}
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t status, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+// CUDA errors: allocation/unsupported failures leave the device usable (the
+// reference classifies them as safe, inference.rs:57-82); anything else makes
+// the execution uncertain and the caller must discard its KV state.
+int32_t cuda_fail(cudaError_t e, const char* what) {
+    const bool safe = e == cudaErrorMemoryAllocation || e == cudaErrorNotSupported ||
+                      e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction;
+    if (safe) return fail(PP_STATUS_PRECONDITION, "%s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+    return fail(PP_STATUS_UNCERTAIN, "EXECUTION_UNCERTAIN: %s failed: %s (%s)", what, cudaGetErrorName(e),
+                cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+    bool ready = false;
+    int num_sms = 0;
+    int major = 0;
+};
+
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int32_t device_info(DeviceInfo& out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(PP_STATUS_PRECONDITION, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    DeviceInfo& d = g_dev[dev];
+    if (!d.ready) {
+        int minor = 0;
+        if ((e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        if ((e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        if (d.major != 10 || minor != 0)
+            return fail(PP_STATUS_PRECONDITION,
+                        "CUDA_ERROR_NO_BINARY_FOR_GPU: this library is built for sm_100a (B200); device is sm_%d%d",
+                        d.major, minor);
+        if ((e = pp::configure_attention_kernels(dev)) != cudaSuccess) return cuda_fail(e, "kernel configuration");
+        if (!g_encode) {
+            void* fn = nullptr;
+            cudaDriverEntryPointQueryResult q{};
+            e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+                return fail(PP_STATUS_PRECONDITION, "CUDA_ERROR_NOT_SUPPORTED: cuTensorMapEncodeTiled unavailable");
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        }
+        d.ready = true;
+    }
+    out = d;
+    return PP_STATUS_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int32_t check_arena(const PpKvArena* a, const char* what) {
+    if (!a) return fail(PP_STATUS_PRECONDITION, "%s: arena is NULL", what);
+    if (a->struct_size < sizeof(PpKvArena)) return fail(PP_STATUS_PRECONDITION, "%s: PpKvArena struct_size too small", what);
+    if (a->rows == 0 || a->heads == 0 || a->rows % a->heads != 0 || a->capacity == 0)
+        return fail(PP_STATUS_PRECONDITION, "INT8 attention geometry differs: rows=%u heads=%u capacity=%u", a->rows,
+                    a->heads, a->capacity);
+    if (a->head_dim != 64 && a->head_dim != 128)
+        return fail(PP_STATUS_PRECONDITION, "INT8 KV requires dense [heads,tokens,64|128], head_dim=%u", a->head_dim);
+    if ((uint64_t)a->rows * a->capacity > 0x7fffff00ull)
+        return fail(PP_STATUS_PRECONDITION, "INT8 KV dimensions overflow: rows*capacity=%llu exceeds 2^31-256",
+                    (unsigned long long)a->rows * a->capacity);
+    if (!a->k || !a->v || !a->k_scale || !a->v_scale) return fail(PP_STATUS_PRECONDITION, "%s: NULL arena pointer", what);
+    if (!aligned(a->k, 16) || !aligned(a->v, 16))
+        return fail(PP_STATUS_PRECONDITION, "%s: packed K/V arenas must be 16-byte aligned", what);
+    if (!aligned(a->k_scale, 4) || !aligned(a->v_scale, 4))
+        return fail(PP_STATUS_PRECONDITION, "%s: scale arenas must be 4-byte aligned", what);
+    return PP_STATUS_OK;
+}
+
+int32_t check_dtype(int32_t t, const char* what) {
+    if (t != PP_DTYPE_F32 && t != PP_DTYPE_BF16) return fail(PP_STATUS_PRECONDITION, "%s: unsupported dtype %d", what, t);
+    return PP_STATUS_OK;
+}
+
+PpAttnParams effective_params(const PpAttnParams* p) {
+    PpAttnParams e{};
+    e.struct_size = sizeof(PpAttnParams);
+    e.q_dtype = PP_DTYPE_F32;
+    e.out_dtype = PP_DTYPE_F32;
+    if (p) {
+        const size_t n = p->struct_size < sizeof(PpAttnParams) ? p->struct_size : sizeof(PpAttnParams);
+        std::memcpy(&e, p, n);
+    }
+    return e;
+}
+
+uint32_t ctas_for(const PpAttnParams& p, const DeviceInfo& d) {
+    uint32_t g = p.max_ctas ? p.max_ctas : (uint32_t)d.num_sms;
+    return g ? g : 1u;
+}
+
+// 2-D map over the packed codes: dims {head_dim, rows*capacity} bytes, boxes of
+// 16 tokens, swizzled so the consumer warps read shared memory conflict-free.
+int32_t encode_codes_map(CUtensorMap* map, const uint8_t* base, const PpKvArena& a) {
+    cuuint64_t dims[2] = {a.head_dim, (cuuint64_t)a.rows * a.capacity};
+    cuuint64_t strides[1] = {a.head_dim};
+    cuuint32_t box[2] = {a.head_dim, 16};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          a.head_dim == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PP_STATUS_PRECONDITION, "cuTensorMapEncodeTiled (codes) failed: %d", (int)r);
+    return PP_STATUS_OK;
+}
+
+// 1-D map over a scale array whose base may be only 4-byte aligned: the map
+// starts at the 16-byte boundary below it and `mis` counts the elements skipped.
+int32_t encode_scale_map(CUtensorMap* map, uint32_t* mis, const float* base, const PpKvArena& a) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(base);
+    const uintptr_t aligned_addr = addr & ~uintptr_t(15);
+    *mis = (uint32_t)((addr - aligned_addr) / 4);
+    cuuint64_t dims[1] = {(cuuint64_t)*mis + (cuuint64_t)a.rows * a.capacity};
+    cuuint64_t strides[1] = {0};
+    cuuint32_t box[1] = {pp::attention_scale_box_elems()};
+    cuuint32_t estr[1] = {1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 1, reinterpret_cast<void*>(aligned_addr), dims, strides,
+                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PP_STATUS_PRECONDITION, "cuTensorMapEncodeTiled (scales) failed: %d", (int)r);
+    return PP_STATUS_OK;
+}
+
+int32_t prepare_launch(const PpKvArena* arena, const PpAttnParams* params, const uint32_t* lengths,
+                       const float* scratch_k, const float* scratch_v, void* workspace, size_t ws_bytes,
+                       pp::AttnLaunch& L, const char* what) {
+    int32_t s;
+    if ((s = check_arena(arena, what))) return s;
+    const PpAttnParams p = effective_params(params);
+    if ((s = check_dtype(p.q_dtype, "q"))) return s;
+    if ((s = check_dtype(p.out_dtype, "out"))) return s;
+    if (!lengths) return fail(PP_STATUS_PRECONDITION, "INT8 attention lengths differ: lengths pointer is NULL");
+    if ((scratch_k == nullptr) != (scratch_v == nullptr))
+        return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be F32[head_rows,1,%u]: pass both or neither", arena->head_dim);
+    if ((scratch_k && !aligned(scratch_k, 4)) || (scratch_v && !aligned(scratch_v, 4)))
+        return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be 4-byte aligned");
+    if (!(p.softmax_scale >= 0.f) || !std::isfinite(p.softmax_scale))
+        return fail(PP_STATUS_PRECONDITION, "softmax_scale must be finite and >= 0");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    L = pp::AttnLaunch{};
+    L.arena = *arena;
+    L.split = p.split_tokens;
+    L.q_dtype = p.q_dtype;
+    L.out_dtype = p.out_dtype;
+    const float scale = p.softmax_scale > 0.f ? p.softmax_scale
+                                              : (arena->head_dim == 64 ? 0.125f : (float)(1.0 / std::sqrt((double)arena->head_dim)));
+    L.scale_log2 = scale * 1.4426950408889634f;
+    L.max_ctas = ctas_for(p, d);
+    L.num_sms = (uint32_t)d.num_sms;
+    L.lengths = lengths;
+    L.scratch_k = scratch_k;
+    L.scratch_v = scratch_v;
+    L.layout = pp::ws_layout(arena->rows, arena->capacity, arena->head_dim, L.split, L.max_ctas);
+    L.plan_ready = (p.flags & PP_ATTN_PLAN_READY) != 0;
+    L.use_pdl = true;
+    if (!workspace) return fail(PP_STATUS_PRECONDITION, "%s: workspace is NULL", what);
+    if (!aligned(workspace, 256)) return fail(PP_STATUS_PRECONDITION, "%s: workspace must be 256-byte aligned", what);
+    if (ws_bytes < L.layout.total)
+        return fail(PP_STATUS_PRECONDITION, "%s: workspace too small (%zu < %zu bytes)", what, ws_bytes, L.layout.total);
+    L.ws = static_cast<unsigned char*>(workspace);
+    return PP_STATUS_OK;
+}
+
+}  // namespace
+
+namespace pp {
+int32_t fail_msg(int32_t status, const char* msg) {
+    g_last_error = msg;
+    return status;
+}
+}  // namespace pp
+
+extern "C" {
+
+uint32_t pp_b200_abi_version(void) { return PP_B200_ABI_VERSION; }
+
+const char* pp_b200_last_error(void) { return g_last_error.c_str(); }
+
+int32_t pp_b200_quantize(const void* x, int32_t x_dtype, uint64_t rows, uint32_t head_dim, uint8_t* packed,
+                         float* scales, uint32_t* status, void* stream) {
+    int32_t s;
+    if (rows == 0 || (head_dim != 64 && head_dim != 128))
+        return fail(PP_STATUS_PRECONDITION, "INT8 KV requires dense [heads,tokens,64|128] (rows=%llu, head_dim=%u)",
+                    (unsigned long long)rows, head_dim);
+    if (rows > (UINT64_MAX / head_dim)) return fail(PP_STATUS_PRECONDITION, "INT8 KV dimensions overflow");
+    if ((s = check_dtype(x_dtype, "quantize input"))) return s;
+    if (!x || !packed || !scales) return fail(PP_STATUS_PRECONDITION, "quantize: NULL pointer");
+    if (!aligned(x, x_dtype == PP_DTYPE_F32 ? 16 : 8) || !aligned(packed, 4) || !aligned(scales, 4))
+        return fail(PP_STATUS_PRECONDITION, "quantize: misaligned pointer");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_quantize(x, x_dtype, rows, head_dim, packed, scales, status, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "INT8 quantize launch");
+}
+
+int32_t pp_b200_dequantize(const uint8_t* packed, const float* scales, uint64_t rows, uint32_t head_dim,
+                           int32_t round_bf16, int32_t out_dtype, void* out, void* stream) {
+    int32_t s;
+    if (rows == 0 || (head_dim != 64 && head_dim != 128))
+        return fail(PP_STATUS_PRECONDITION, "INT8 KV scales differ: rows=%llu head_dim=%u", (unsigned long long)rows, head_dim);
+    if ((s = check_dtype(out_dtype, "dequantize output"))) return s;
+    if (!packed || !scales || !out) return fail(PP_STATUS_PRECONDITION, "dequantize: NULL pointer");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_dequantize(packed, scales, rows, head_dim, round_bf16, out_dtype, out, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "INT8 dequantize launch");
+}
+
+int32_t pp_b200_quant_append(const PpKvArena* arena, const void* k_new, const void* v_new, int32_t dtype,
+                             const uint32_t* offsets, uint32_t commit, uint32_t* status, void* stream) {
+    int32_t s;
+    if ((s = check_arena(arena, "quant_append"))) return s;
+    if ((s = check_dtype(dtype, "append input"))) return s;
+    if (!k_new || !v_new || !offsets) return fail(PP_STATUS_PRECONDITION, "INT8 batch requires [B,H,1,D] scratch: NULL input");
+    const uintptr_t need = dtype == PP_DTYPE_F32 ? 16 : 8;
+    if (!aligned(k_new, need) || !aligned(v_new, need)) return fail(PP_STATUS_PRECONDITION, "quant_append: misaligned K/V input");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_quant_append(*arena, k_new, v_new, dtype, offsets, commit, status, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "INT8 quant_append launch");
+}
+
+int32_t pp_b200_copy_prefix(const PpKvArena* src, const PpKvArena* dst, const uint32_t* lengths, void* stream) {
+    int32_t s;
+    if ((s = check_arena(src, "copy_prefix src"))) return s;
+    if ((s = check_arena(dst, "copy_prefix dst"))) return s;
+    if (src->rows != dst->rows || src->heads != dst->heads || src->head_dim != dst->head_dim)
+        return fail(PP_STATUS_PRECONDITION, "batch KV existing row is incompatible: arenas differ in rows/heads/head_dim");
+    if (!lengths) return fail(PP_STATUS_PRECONDITION, "copy_prefix: lengths is NULL");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_copy_prefix(*src, *dst, lengths, nullptr, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "INT8 copy_prefix launch");
+}
+
+size_t pp_b200_attention_workspace_size(const PpKvArena* arena, const PpAttnParams* params) {
+    if (!arena || arena->rows == 0 || (arena->head_dim != 64 && arena->head_dim != 128)) return 0;
+    const PpAttnParams p = effective_params(params);
+    uint32_t g = p.max_ctas;
+    if (!g) {
+        DeviceInfo d;
+        if (device_info(d) != PP_STATUS_OK) g = 1024;  // conservative without a device
+        else g = (uint32_t)d.num_sms;
+    }
+    return pp::ws_layout(arena->rows, arena->capacity, arena->head_dim, p.split_tokens, g).total;
+}
+
+int32_t pp_b200_plan_ragged(const PpKvArena* arena, const PpAttnParams* params, const uint32_t* lengths,
+                            uint32_t scratch_token, void* workspace, size_t workspace_bytes, void* stream) {
+    pp::AttnLaunch L;
+    static const float kDummy = 0.f;
+    const float* sk = scratch_token ? &kDummy : nullptr;  // only its presence matters to the plan
+    int32_t s = prepare_launch(arena, params, lengths, sk, sk, workspace, workspace_bytes, L, "plan_ragged");
+    if (s) return s;
+    cudaError_t e = pp::launch_plan(L, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "INT8 plan launch");
+}
+
+int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* params, const void* q,
+                                 const float* scratch_k, const float* scratch_v, const uint32_t* lengths, void* out,
+                                 void* workspace, size_t workspace_bytes, uint32_t* status, void* stream) {
+    pp::AttnLaunch L;
+    int32_t s = prepare_launch(arena, params, lengths, scratch_k, scratch_v, workspace, workspace_bytes, L,
+                               "decode_attention");
+    if (s) return s;
+    if (!q || !out) return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be F32[head_rows,1,%u]: NULL q/out", arena->head_dim);
+    if (!aligned(q, 16)) return fail(PP_STATUS_PRECONDITION, "decode_attention: q must be 16-byte aligned");
+    if (!aligned(out, L.out_dtype == PP_DTYPE_F32 ? 4 : 2))
+        return fail(PP_STATUS_PRECONDITION, "decode_attention: out is misaligned");
+    L.q = q;
+    L.out = out;
+    L.status = status;
+    if ((s = encode_codes_map(&L.map_k, arena->k, *arena))) return s;
+    if ((s = encode_codes_map(&L.map_v, arena->v, *arena))) return s;
+    if ((s = encode_scale_map(&L.map_ks, &L.ks_mis, arena->k_scale, *arena))) return s;
+    if ((s = encode_scale_map(&L.map_vs, &L.vs_mis, arena->v_scale, *arena))) return s;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    if (!L.plan_ready && (e = pp::launch_plan(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 plan launch");
+    if ((e = pp::launch_attention(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 attention launch");
+    if ((e = pp::launch_combine(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 combine launch");
+    return PP_STATUS_OK;
+}
+
+const char* pp_b200_status_message(uint32_t bits) {
+    if (bits == 0) return "ok";
+    if (bits & PP_DEV_WAIT_TIMEOUT) return "EXECUTION_UNCERTAIN: a bounded device pipeline wait timed out";
+    if (bits & PP_DEV_NONFINITE_INPUT) return "non-finite INT8 KV input";
+    if (bits & PP_DEV_OFFSET_RANGE) return "batch KV needs context rebuild: append offset outside capacity";
+    if (bits & PP_DEV_LENGTH_RANGE) return "INT8 attention lengths differ: length exceeds capacity (row output is NaN)";
+    return "unknown device status";
+}
+
+}  // extern "C"

@@ -1,0 +1,114 @@
+// Internal declarations shared by the kernels and the C ABI implementation.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../../include/pp_b200.h"
+
+namespace pp {
+
+// ----------------------------------------------------------- attention plan
+//
+// Workspace layout (all offsets from the workspace base, 256-byte aligned):
+//   PlanHeader                                    @ 0
+//   row_len   u32 [rows]      history tokens per row, kInvalidRow if invalid
+//   row_seg   u32 [rows + 1]  first segment of each row (segments are row-sorted)
+//   cta_seg   u32 [max_ctas + 1]  first segment of each CTA
+//   segs      SegDesc [max_segs]
+//   partials  f32 [max_segs][head_dim + 4]   acc[0..D), m (log2 units), z
+// A segment is a contiguous token range of one row processed by one CTA and
+// producing one partial (m, z, acc) for the log-sum-exp combine.
+
+constexpr uint32_t kInvalidRow = 0xffffffffu;
+
+struct PlanHeader {
+    unsigned long long total_tokens;
+    unsigned long long tokens_per_cta;
+    uint32_t n_segs;
+    uint32_t n_ctas;
+    uint32_t rows;
+    uint32_t heads;
+    uint32_t capacity;
+    uint32_t split;
+    uint32_t scratch;
+    uint32_t max_segs;
+    uint32_t max_ctas;
+    uint32_t pad[3];
+};
+
+struct SegDesc {
+    uint32_t row, t0, t1, pad;
+};
+
+struct WsLayout {
+    size_t row_len, row_seg, cta_seg, segs, partials, total;
+    uint32_t max_segs, max_ctas;
+};
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Stream-K segments: at most one per row plus one per CTA boundary.
+// Fixed split: at most ceil(capacity / split) per row.
+inline WsLayout ws_layout(uint32_t rows, uint32_t capacity, uint32_t head_dim, uint32_t split, uint32_t max_ctas) {
+    WsLayout l{};
+    l.max_ctas = max_ctas;
+    uint64_t segs = split ? (uint64_t)rows * ((capacity + split - 1) / split) : (uint64_t)rows + max_ctas;
+    if (segs == 0) segs = 1;
+    l.max_segs = (uint32_t)(segs > 0xffffffffull ? 0xffffffffull : segs);
+    size_t off = align_up(sizeof(PlanHeader), 256);
+    l.row_len = off;
+    off = align_up(off + 4ull * rows, 256);
+    l.row_seg = off;
+    off = align_up(off + 4ull * (rows + 1), 256);
+    l.cta_seg = off;
+    off = align_up(off + 4ull * (max_ctas + 1), 256);
+    l.segs = off;
+    off = align_up(off + sizeof(SegDesc) * (size_t)l.max_segs, 256);
+    l.partials = off;
+    off = align_up(off + 4ull * (head_dim + 4) * (size_t)l.max_segs, 256);
+    l.total = off;
+    return l;
+}
+
+struct AttnLaunch {
+    PpKvArena arena;
+    uint32_t split;
+    int q_dtype, out_dtype;
+    float scale_log2;     // softmax scale * log2(e)
+    uint32_t max_ctas;    // grid of the attention kernel
+    uint32_t num_sms;
+    const void* q;
+    const float* scratch_k;
+    const float* scratch_v;
+    const uint32_t* lengths;
+    void* out;
+    unsigned char* ws;
+    WsLayout layout;
+    uint32_t* status;
+    bool plan_ready;
+    bool use_pdl;
+    // Tensor maps (host-encoded) for K, V codes and K, V scales.
+    CUtensorMap map_k, map_v, map_ks, map_vs;
+    uint32_t ks_mis, vs_mis;  // element offset of the scale arrays inside their maps
+};
+
+cudaError_t launch_quantize(const void* x, int dtype, uint64_t rows, uint32_t d, uint8_t* packed, float* scales,
+                            uint32_t* status, cudaStream_t stream);
+cudaError_t launch_quant_append(const PpKvArena& a, const void* k_new, const void* v_new, int dtype,
+                                const uint32_t* offsets, uint32_t commit, uint32_t* status, cudaStream_t stream);
+cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, uint64_t rows, uint32_t d, int round_bf16,
+                              int out_dtype, void* out, cudaStream_t stream);
+cudaError_t launch_copy_prefix(const PpKvArena& s, const PpKvArena& d, const uint32_t* lengths, uint32_t* status,
+                               cudaStream_t stream);
+cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream);
+cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream);
+cudaError_t launch_combine(const AttnLaunch& L, cudaStream_t stream);
+cudaError_t configure_attention_kernels(int device);
+
+// Records `msg` as the calling thread's last error and returns `status`.
+int32_t fail_msg(int32_t status, const char* msg);
+
+}  // namespace pp

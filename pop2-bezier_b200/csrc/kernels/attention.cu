@@ -1,0 +1,809 @@
+// Int8 historical-KV decode attention for sm_100a.
+//
+// Replaces the reference's pp_i8_attention + pp_i8_merge (app/src/model/
+// int8_kv.cu:28-59).  Same arithmetic contract:
+//   k_t = bf16(i8 * ks[t]), v_t = bf16(i8 * vs[t])          (pp_i8_load, :23-27)
+//   score_t = (q . k_t) * scale,  p_t = exp(score_t - max),  out = sum p v / sum p
+//   reference mode: the token at index `past` is the f32 scratch (sk, sv), :36-37,49
+// Different machinery:
+//   * plan_kernel turns device lengths into a stream-K segment list (every CTA
+//     gets the same number of tokens whatever the raggedness), or into
+//     fixed-size splits when the caller asks for the reference's split_tokens.
+//   * attn_kernel is persistent, one CTA per SM: a producer warp streams
+//     16-token boxes of int8 K/V (TMA, 128B/64B swizzle) and their scales into
+//     a multi-stage shared-memory ring guarded by mbarriers; eight consumer
+//     warps dequantize to bf16 in registers and run the two dot products
+//     (q.k and p.V) on the tensor cores (mma.sync m16n8k16, f32 accumulate),
+//     with q and p split into three bf16 terms so the products are exact in f32.
+//   * combine_kernel merges the per-segment partials (and, in reference mode,
+//     the scratch token) with a log-sum-exp combine.
+// All softmax arithmetic runs in base 2 (scores pre-scaled by log2 e).
+#include "common.cuh"
+#include "../host/internal.h"
+
+namespace pp {
+namespace {
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: generous, never hit in normal runs
+
+// ------------------------------------------------------------------ plan
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_tot, uint32_t& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = (lane < (int)(blockDim.x >> 5)) ? warp_tot[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_tot[lane] = w;  // inclusive
+    }
+    __syncthreads();
+    const uint32_t before = (warp ? warp_tot[warp - 1] : 0u) + x - v;
+    total = warp_tot[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return before;
+}
+
+struct PlanArgs {
+    const uint32_t* lengths;
+    unsigned char* ws;
+    WsLayout l;
+    uint32_t rows, heads, capacity, split, scratch, max_ctas, min_tokens;
+    uint32_t* status;
+};
+
+__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
+    __shared__ uint32_t warp_tot[32];
+    __shared__ uint32_t s_n_ctas, s_per_cta, s_total, s_bad;
+    PlanHeader* hdr = reinterpret_cast<PlanHeader*>(a.ws);
+    uint32_t* row_len = reinterpret_cast<uint32_t*>(a.ws + a.l.row_len);
+    uint32_t* row_seg = reinterpret_cast<uint32_t*>(a.ws + a.l.row_seg);
+    uint32_t* cta_seg = reinterpret_cast<uint32_t*>(a.ws + a.l.cta_seg);
+    SegDesc* segs = reinterpret_cast<SegDesc*>(a.ws + a.l.segs);
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+
+    auto history = [&](uint32_t r, bool& valid) -> uint32_t {
+        uint32_t len = __ldg(a.lengths + r / a.heads);
+        valid = a.scratch ? (len <= a.capacity) : (len > 0 && len <= a.capacity);
+        return valid ? len : 0u;
+    };
+
+    // Pass 1: per-row history lengths and the total token count.
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < a.rows; base += blockDim.x) {
+        const uint32_t r = base + threadIdx.x;
+        bool valid = true;
+        uint32_t h = r < a.rows ? history(r, valid) : 0u;
+        if (r < a.rows) {
+            row_len[r] = valid ? h : kInvalidRow;
+            if (!valid) s_bad = 1;
+        }
+        uint32_t tot;
+        block_exclusive_scan(h, warp_tot, tot);
+        carry += tot;
+    }
+    if (threadIdx.x == 0) {
+        const uint32_t total = carry;
+        uint32_t n_ctas = 0, per = 0;
+        if (total) {
+            if (a.split) {
+                n_ctas = a.max_ctas;  // refined after the segment count is known
+            } else {
+                uint32_t want = (total + a.min_tokens - 1) / a.min_tokens;
+                n_ctas = want < a.max_ctas ? want : a.max_ctas;
+                per = (total + n_ctas - 1) / n_ctas;
+                n_ctas = (total + per - 1) / per;  // every CTA range non-empty
+            }
+        }
+        s_n_ctas = n_ctas;
+        s_per_cta = per;
+        s_total = total;
+        if (s_bad && a.status) atomicOr(a.status, PP_DEV_LENGTH_RANGE);
+    }
+    __syncthreads();
+    const uint32_t per = s_per_cta;
+
+    // Pass 2: token prefix -> segment counts -> segment prefix -> descriptors.
+    uint32_t tok_carry = 0, seg_carry = 0;
+    for (uint32_t base = 0; base < a.rows; base += blockDim.x) {
+        const uint32_t r = base + threadIdx.x;
+        bool valid = true;
+        const uint32_t h = r < a.rows ? history(r, valid) : 0u;
+        uint32_t tot;
+        const uint32_t p0 = tok_carry + block_exclusive_scan(h, warp_tot, tot);
+        tok_carry += tot;
+        uint32_t n = 0;
+        if (h) {
+            if (a.split) n = (h + a.split - 1) / a.split;
+            else n = (p0 + h - 1) / per - p0 / per + 1;
+        }
+        const uint32_t s0 = seg_carry + block_exclusive_scan(n, warp_tot, tot);
+        seg_carry += tot;
+        if (r < a.rows) {
+            row_seg[r] = s0;
+            if (a.split) {
+                for (uint32_t k = 0; k < n; ++k) {
+                    uint32_t t0 = k * a.split, t1 = min(h, t0 + a.split);
+                    segs[s0 + k] = SegDesc{r, t0, t1, 0u};
+                }
+            } else if (n) {
+                const uint32_t j0 = p0 / per;
+                for (uint32_t k = 0; k < n; ++k) {
+                    const uint32_t j = j0 + k;
+                    const uint32_t lo = max(p0, j * per), hi = min(p0 + h, (j + 1) * per);
+                    segs[s0 + k] = SegDesc{r, lo - p0, hi - p0, 0u};
+                    if (j * per >= p0) cta_seg[j] = s0 + k;  // CTA j starts inside this row
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) row_seg[a.rows] = seg_carry;
+    uint32_t n_ctas = s_n_ctas;
+    if (a.split) {
+        n_ctas = seg_carry < a.max_ctas ? seg_carry : a.max_ctas;
+        for (uint32_t j = threadIdx.x; j <= n_ctas; j += blockDim.x)
+            cta_seg[j] = n_ctas ? (uint32_t)(((unsigned long long)j * seg_carry) / n_ctas) : 0u;
+    } else if (threadIdx.x == 0) {
+        cta_seg[n_ctas] = seg_carry;
+        if (n_ctas == 0) cta_seg[0] = 0;
+    }
+    if (threadIdx.x == 0) {
+        hdr->total_tokens = s_total;
+        hdr->tokens_per_cta = per;
+        hdr->n_segs = seg_carry;
+        hdr->n_ctas = n_ctas;
+        hdr->rows = a.rows;
+        hdr->heads = a.heads;
+        hdr->capacity = a.capacity;
+        hdr->split = a.split;
+        hdr->scratch = a.scratch;
+        hdr->max_segs = a.l.max_segs;
+        hdr->max_ctas = a.max_ctas;
+    }
+}
+
+// ------------------------------------------------------------- attention
+
+template <int D>
+struct Cfg {
+    static constexpr int NC = 8;                    // consumer warps
+    static constexpr int THREADS = (NC + 1) * 32;   // + one producer warp
+    static constexpr int BOX = 16;                  // tokens per TMA box = one consumer warp's slice
+    static constexpr int T = BOX * NC;              // tokens per stage
+    static constexpr int KV_BYTES = T * D;
+    static constexpr int SC_BOX = T + 4;            // scale elements per stage (+ alignment slack)
+    static constexpr int SC_BYTES = SC_BOX * 4;
+    static constexpr int Q_BYTES = D * 4;
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = KV_BYTES;
+    static constexpr int OFF_KS = 2 * KV_BYTES;
+    static constexpr int SC_SLOT = ((SC_BYTES + 127) / 128) * 128;  // tensor copies land 128B-aligned
+    static constexpr int OFF_VS = OFF_KS + SC_SLOT;
+    static constexpr int OFF_Q = OFF_VS + SC_SLOT;
+    static constexpr int OFF_META = OFF_Q + Q_BYTES;
+    static constexpr int STAGE_BYTES = ((OFF_META + 32 + 1023) / 1024) * 1024;
+    static constexpr int STAGES = D == 128 ? 5 : 8;
+    static constexpr int RED_FLOATS = NC * (D + 4);
+    static constexpr int OFF_RED = STAGES * STAGE_BYTES;
+    static constexpr int OFF_BAR = OFF_RED + 2 * RED_FLOATS * 4;
+    static constexpr int BAR_COUNT = 2 * STAGES + 2;
+    static constexpr int SMEM_BYTES = OFF_BAR + BAR_COUNT * 8 + 16 + 1024;  // + abort flag + base alignment
+    static constexpr int NI = D / 16;  // q.k MMAs per 16-token block (k = 16 channels each)
+    static constexpr int NJ = D / 16;  // p.V MMAs per 16-token block (m = 16 channels each)
+};
+
+struct StageMeta {
+    uint32_t row, t, nvalid, slot, flags, ks_off, vs_off, pad;
+};
+constexpr uint32_t kFirst = 1u, kLast = 2u, kTerm = 4u;
+
+struct AttnArgs {
+    const void* q;
+    const unsigned char* ws;
+    float* partials;
+    WsLayout l;
+    uint32_t capacity;
+    uint32_t ks_mis, vs_mis;
+    float scale_log2;
+    uint32_t* status;
+};
+
+template <typename QT>
+__device__ __forceinline__ void load_q_vals(uint32_t q_smem, int c0, int n, float* out);
+
+// Channels [c0, c0+n) of the staged q row (f32).
+template <>
+__device__ __forceinline__ void load_q_vals<float>(uint32_t q_smem, int c0, int n, float* out) {
+    for (int i = 0; i < n; i += 4) {
+        uint4 v = lds128(q_smem + (uint32_t)(c0 + i) * 4u);
+        out[i] = __uint_as_float(v.x);
+        out[i + 1] = __uint_as_float(v.y);
+        out[i + 2] = __uint_as_float(v.z);
+        out[i + 3] = __uint_as_float(v.w);
+    }
+}
+template <>
+__device__ __forceinline__ void load_q_vals<__nv_bfloat16>(uint32_t q_smem, int c0, int n, float* out) {
+    for (int i = 0; i < n; i += 8) {
+        uint4 v = lds128(q_smem + (uint32_t)(c0 + i) * 2u);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            out[i + 2 * k] = bf16_lo_to_f32(w[k]);
+            out[i + 2 * k + 1] = bf16_hi_to_f32(w[k]);
+        }
+    }
+}
+
+// bf16 term `part` (0: hi, 1: lo, 2: lo2, else 0) of the exact three-term
+// split of two f32 values, packed.  hi + lo + lo2 == x exactly for normal x.
+__device__ __forceinline__ uint32_t split_term_pack(float a, float b, int part) {
+    const uint32_t h = pack_bf16x2(a, b);
+    const float ra = a - bf16_lo_to_f32(h), rb = b - bf16_hi_to_f32(h);
+    const uint32_t l = pack_bf16x2(ra, rb);
+    const uint32_t l2 = pack_bf16x2(ra - bf16_lo_to_f32(l), rb - bf16_hi_to_f32(l));
+    return part == 0 ? h : part == 1 ? l : part == 2 ? l2 : 0u;
+}
+
+template <int D, typename QT>
+__global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                const __grid_constant__ CUtensorMap map_ks, const __grid_constant__ CUtensorMap map_vs,
+                const AttnArgs args) {
+    using C = Cfg<D>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* red_bar = empty + C::STAGES;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 2);
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], C::NC);
+        }
+        mbar_init(&red_bar[0], C::NC);
+        mbar_init(&red_bar[1], C::NC);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == C::NC && lane == 0) {
+        tma_prefetch_desc(&map_k);
+        tma_prefetch_desc(&map_v);
+        tma_prefetch_desc(&map_ks);
+        tma_prefetch_desc(&map_vs);
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait_primary();  // the plan (previous kernel) is complete and visible
+
+    const PlanHeader* hdr = reinterpret_cast<const PlanHeader*>(args.ws);
+    const uint32_t* cta_seg = reinterpret_cast<const uint32_t*>(args.ws + args.l.cta_seg);
+    const SegDesc* segs = reinterpret_cast<const SegDesc*>(args.ws + args.l.segs);
+
+    if (warp == C::NC) {
+        // ------------------------------------------------------ producer
+        if (lane != 0) return;
+        const uint32_t n_ctas = hdr->n_ctas;
+        uint32_t s_begin = 0, s_end = 0;
+        if (blockIdx.x < n_ctas) {
+            s_begin = cta_seg[blockIdx.x];
+            s_end = cta_seg[blockIdx.x + 1];
+        }
+        constexpr uint32_t q_bytes = D * sizeof(QT);
+        uint32_t it = 0;
+        bool ok = true;
+        SegDesc next = s_begin < s_end ? segs[s_begin] : SegDesc{0, 0, 0, 0};
+        for (uint32_t s = s_begin; s < s_end && ok; ++s) {
+            const SegDesc sd = next;
+            if (s + 1 < s_end) next = segs[s + 1];
+            for (uint32_t t = sd.t0; t < sd.t1; t += C::T, ++it) {
+                const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
+                if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, kWaitLimitNs)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = smem + slot * C::STAGE_BYTES;
+                const uint32_t n = min((uint32_t)C::T, sd.t1 - t);
+                const uint32_t nbox = (n + C::BOX - 1) / C::BOX;
+                const uint32_t tok = sd.row * args.capacity + t;
+                const uint32_t ksx = (args.ks_mis + tok) & ~3u, vsx = (args.vs_mis + tok) & ~3u;
+                StageMeta* meta = reinterpret_cast<StageMeta*>(st + C::OFF_META);
+                const bool first = t == sd.t0, last = t + C::T >= sd.t1;
+                meta->row = sd.row;
+                meta->t = t;
+                meta->nvalid = n;
+                meta->slot = s;
+                meta->flags = (first ? kFirst : 0u) | (last ? kLast : 0u);
+                meta->ks_off = args.ks_mis + tok - ksx;
+                meta->vs_off = args.vs_mis + tok - vsx;
+                const uint32_t bytes = nbox * C::BOX * D * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                for (uint32_t b = 0; b < nbox; ++b) {
+                    tma_load_2d(st + C::OFF_K + b * C::BOX * D, &map_k, &full[slot], 0, (int32_t)(tok + b * C::BOX));
+                    tma_load_2d(st + C::OFF_V + b * C::BOX * D, &map_v, &full[slot], 0, (int32_t)(tok + b * C::BOX));
+                }
+                tma_load_1d(st + C::OFF_KS, &map_ks, &full[slot], (int32_t)ksx);
+                tma_load_1d(st + C::OFF_VS, &map_vs, &full[slot], (int32_t)vsx);
+                if (first) {
+                    const unsigned char* qrow = reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * q_bytes;
+                    bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
+                }
+            }
+        }
+        if (ok) {
+            const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
+            if (mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, kWaitLimitNs)) {
+                StageMeta* meta = reinterpret_cast<StageMeta*>(smem + slot * C::STAGE_BYTES + C::OFF_META);
+                meta->flags = kTerm;
+                mbar_arrive(&full[slot]);
+                return;
+            }
+        }
+        // Abort: report, then wait (bounded) for the copies this warp issued.
+        *abort_flag = 1;
+        if (args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+        const uint32_t lo = it > (uint32_t)C::STAGES ? it - C::STAGES : 0u;
+        for (uint32_t i = lo; i < it; ++i) {
+            volatile int never = 0;
+            mbar_wait_bounded(&full[i % C::STAGES], (i / C::STAGES) & 1u, &never, kWaitLimitNs);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- consumers
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t qb[C::NI][2];
+    float acc[C::NJ][4];
+    float m2 = -INFINITY, zsum = 0.f;
+#pragma unroll
+    for (int j = 0; j < C::NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll
+    for (int i = 0; i < C::NI; ++i) qb[i][0] = qb[i][1] = 0u;
+    uint32_t red_phase[2] = {0u, 0u};
+    uint32_t seg_count = 0;
+    float* partials = args.partials;
+
+    for (uint32_t it = 0;; ++it) {
+        const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
+        if (!mbar_wait_bounded(&full[slot], ph, abort_flag, kWaitLimitNs)) {
+            *abort_flag = 1;
+            if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+            return;
+        }
+        unsigned char* st = smem + slot * C::STAGE_BYTES;
+        const StageMeta meta = *reinterpret_cast<const StageMeta*>(st + C::OFF_META);
+        if (meta.flags & kTerm) break;
+
+        if (meta.flags & kFirst) {
+            // q row -> three-term bf16 B fragments for channel slice of thread c.
+            constexpr int QN = D / 4;  // channels per thread: [QN*c, QN*c + QN)
+            float qv[QN];
+            load_q_vals<QT>(smem_addr(st + C::OFF_Q), QN * c, QN, qv);
+#pragma unroll
+            for (int i = 0; i < C::NI; ++i) {
+                const float a0 = qv[4 * i] * args.scale_log2, a1 = qv[4 * i + 1] * args.scale_log2;
+                const float a2 = qv[4 * i + 2] * args.scale_log2, a3 = qv[4 * i + 3] * args.scale_log2;
+                qb[i][0] = split_term_pack(a0, a1, g);
+                qb[i][1] = split_term_pack(a2, a3, g);
+            }
+            m2 = -INFINITY;
+            zsum = 0.f;
+#pragma unroll
+            for (int j = 0; j < C::NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        }
+
+        const int tok0 = warp * C::BOX;
+        const int nv = (int)meta.nvalid - tok0;
+        if (nv > 0) {
+            const uint32_t kt = smem_addr(st + C::OFF_K + tok0 * D);
+            const uint32_t vt = smem_addr(st + C::OFF_V + tok0 * D);
+            const uint32_t ks = smem_addr(st + C::OFF_KS) + (meta.ks_off + tok0) * 4u;
+            const uint32_t vs = smem_addr(st + C::OFF_VS) + (meta.vs_off + tok0) * 4u;
+
+            // ---- scores: q . k for tokens g and g+8 of this warp's box
+            const float sg = g < nv ? lds_f32(ks + g * 4) : 0.f;
+            const float sg8 = g + 8 < nv ? lds_f32(ks + (g + 8) * 4) : 0.f;
+            float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (D == 128) {
+                // 128B swizzle: row e, 16B chunk x stored at chunk x ^ (e & 7).
+                const uint4 ka0 = lds128(kt + g * 128 + (((2 * c) ^ g) << 4));
+                const uint4 ka1 = lds128(kt + g * 128 + (((2 * c + 1) ^ g) << 4));
+                const uint4 kb0 = lds128(kt + (g + 8) * 128 + (((2 * c) ^ g) << 4));
+                const uint4 kb1 = lds128(kt + (g + 8) * 128 + (((2 * c + 1) ^ g) << 4));
+                const uint32_t wa[8] = {ka0.x, ka0.y, ka0.z, ka0.w, ka1.x, ka1.y, ka1.z, ka1.w};
+                const uint32_t wb[8] = {kb0.x, kb0.y, kb0.z, kb0.w, kb1.x, kb1.y, kb1.z, kb1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float a0, a1, a2, a3, b0, b1, b2, b3;
+                    i8x4_to_f32(wa[i], a0, a1, a2, a3);
+                    i8x4_to_f32(wb[i], b0, b1, b2, b3);
+                    mma_bf16_16816(sacc, pack_bf16x2(a0 * sg, a1 * sg), pack_bf16x2(b0 * sg8, b1 * sg8),
+                                   pack_bf16x2(a2 * sg, a3 * sg), pack_bf16x2(b2 * sg8, b3 * sg8), qb[i][0],
+                                   qb[i][1]);
+                }
+            } else {
+                // 64B swizzle: row e, 16B chunk x stored at chunk x ^ ((e >> 1) & 3).
+                const int sw = (g >> 1) & 3;
+                const uint4 ka = lds128(kt + g * 64 + ((c ^ sw) << 4));
+                const uint4 kb = lds128(kt + (g + 8) * 64 + ((c ^ sw) << 4));
+                const uint32_t wa[4] = {ka.x, ka.y, ka.z, ka.w};
+                const uint32_t wb[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float a0, a1, a2, a3, b0, b1, b2, b3;
+                    i8x4_to_f32(wa[i], a0, a1, a2, a3);
+                    i8x4_to_f32(wb[i], b0, b1, b2, b3);
+                    mma_bf16_16816(sacc, pack_bf16x2(a0 * sg, a1 * sg), pack_bf16x2(b0 * sg8, b1 * sg8),
+                                   pack_bf16x2(a2 * sg, a3 * sg), pack_bf16x2(b2 * sg8, b3 * sg8), qb[i][0],
+                                   qb[i][1]);
+                }
+            }
+            float s_g = sacc[0] + sacc[1];
+            float s_g8 = sacc[2] + sacc[3];
+            s_g += __shfl_xor_sync(0xffffffffu, s_g, 1);
+            s_g8 += __shfl_xor_sync(0xffffffffu, s_g8, 1);
+            s_g += __shfl_xor_sync(0xffffffffu, s_g, 2);
+            s_g8 += __shfl_xor_sync(0xffffffffu, s_g8, 2);
+            if (g >= nv) s_g = -INFINITY;
+            if (g + 8 >= nv) s_g8 = -INFINITY;
+
+            // ---- online softmax (base 2)
+            float bm = fmaxf(s_g, s_g8);
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+            if (bm > m2) {
+                const float alpha = fast_exp2(m2 - bm);
+                zsum *= alpha;
+#pragma unroll
+                for (int j = 0; j < C::NJ; ++j) {
+                    acc[j][0] *= alpha;
+                    acc[j][1] *= alpha;
+                    acc[j][2] *= alpha;
+                    acc[j][3] *= alpha;
+                }
+                m2 = bm;
+            }
+            const float p_g = fast_exp2(s_g - m2), p_g8 = fast_exp2(s_g8 - m2);
+            zsum += p_g + p_g8;
+
+            // ---- p as the B operand: tokens 2c, 2c+1, 2c+8, 2c+9, term g
+            const float x0 = __shfl_sync(0xffffffffu, p_g, 8 * c);
+            const float x1 = __shfl_sync(0xffffffffu, p_g, 8 * c + 4);
+            const float x2 = __shfl_sync(0xffffffffu, p_g8, 8 * c);
+            const float x3 = __shfl_sync(0xffffffffu, p_g8, 8 * c + 4);
+            const uint32_t pb0 = split_term_pack(x0, x1, g);
+            const uint32_t pb1 = split_term_pack(x2, x3, g);
+
+            // ---- p . V: A = V^T (rows = channels, k = tokens 2c, 2c+1, 2c+8, 2c+9)
+            const int e0 = 2 * c, e1 = 2 * c + 1, e2 = 2 * c + 8, e3 = 2 * c + 9;
+            const float v0s = e0 < nv ? lds_f32(vs + e0 * 4) : 0.f;
+            const float v1s = e1 < nv ? lds_f32(vs + e1 * 4) : 0.f;
+            const float v2s = e2 < nv ? lds_f32(vs + e2 * 4) : 0.f;
+            const float v3s = e3 < nv ? lds_f32(vs + e3 * 4) : 0.f;
+            if constexpr (D == 128) {
+                // thread holds channels [16g, 16g+16) of its four tokens
+                const uint4 v0 = lds128(vt + e0 * 128 + ((g ^ e0) << 4));
+                const uint4 v1 = lds128(vt + e1 * 128 + ((g ^ e1) << 4));
+                const uint4 v2 = lds128(vt + e2 * 128 + ((g ^ (e2 & 7)) << 4));
+                const uint4 v3 = lds128(vt + e3 * 128 + ((g ^ (e3 & 7)) << 4));
+                const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
+                const uint32_t w2[4] = {v2.x, v2.y, v2.z, v2.w}, w3[4] = {v3.x, v3.y, v3.z, v3.w};
+#pragma unroll
+                for (int jw = 0; jw < 2; ++jw) {
+                    float a[4][4], b[4][4];  // [token][elem]: a = channels 16g+4jw+e, b = +8
+                    i8x4_to_f32(w0[jw], a[0][0], a[0][1], a[0][2], a[0][3]);
+                    i8x4_to_f32(w1[jw], a[1][0], a[1][1], a[1][2], a[1][3]);
+                    i8x4_to_f32(w2[jw], a[2][0], a[2][1], a[2][2], a[2][3]);
+                    i8x4_to_f32(w3[jw], a[3][0], a[3][1], a[3][2], a[3][3]);
+                    i8x4_to_f32(w0[2 + jw], b[0][0], b[0][1], b[0][2], b[0][3]);
+                    i8x4_to_f32(w1[2 + jw], b[1][0], b[1][1], b[1][2], b[1][3]);
+                    i8x4_to_f32(w2[2 + jw], b[2][0], b[2][1], b[2][2], b[2][3]);
+                    i8x4_to_f32(w3[2 + jw], b[3][0], b[3][1], b[3][2], b[3][3]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        mma_bf16_16816(acc[4 * jw + e], pack_bf16x2(a[0][e] * v0s, a[1][e] * v1s),
+                                       pack_bf16x2(b[0][e] * v0s, b[1][e] * v1s),
+                                       pack_bf16x2(a[2][e] * v2s, a[3][e] * v3s),
+                                       pack_bf16x2(b[2][e] * v2s, b[3][e] * v3s), pb0, pb1);
+                    }
+                }
+            } else {
+                // thread holds channels [8g, 8g+8) of its four tokens
+                const uint32_t off = ((((uint32_t)g >> 1) ^ (uint32_t)c) << 4) + (((uint32_t)g & 1u) << 3);
+                const uint2 v0 = lds64(vt + e0 * 64 + off);
+                const uint2 v1 = lds64(vt + e1 * 64 + off);
+                const uint2 v2 = lds64(vt + e2 * 64 + off);
+                const uint2 v3 = lds64(vt + e3 * 64 + off);
+                float a[4][4], b[4][4];
+                i8x4_to_f32(v0.x, a[0][0], a[0][1], a[0][2], a[0][3]);
+                i8x4_to_f32(v1.x, a[1][0], a[1][1], a[1][2], a[1][3]);
+                i8x4_to_f32(v2.x, a[2][0], a[2][1], a[2][2], a[2][3]);
+                i8x4_to_f32(v3.x, a[3][0], a[3][1], a[3][2], a[3][3]);
+                i8x4_to_f32(v0.y, b[0][0], b[0][1], b[0][2], b[0][3]);
+                i8x4_to_f32(v1.y, b[1][0], b[1][1], b[1][2], b[1][3]);
+                i8x4_to_f32(v2.y, b[2][0], b[2][1], b[2][2], b[2][3]);
+                i8x4_to_f32(v3.y, b[3][0], b[3][1], b[3][2], b[3][3]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    mma_bf16_16816(acc[e], pack_bf16x2(a[0][e] * v0s, a[1][e] * v1s),
+                                   pack_bf16x2(b[0][e] * v0s, b[1][e] * v1s),
+                                   pack_bf16x2(a[2][e] * v2s, a[3][e] * v3s),
+                                   pack_bf16x2(b[2][e] * v2s, b[3][e] * v3s), pb0, pb1);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+
+        if (meta.flags & kLast) {
+            // ---- segment epilogue: merge the NC warp states into one partial
+            const uint32_t par = seg_count & 1u;
+            float* buf = red + par * C::RED_FLOATS;
+            float* mine = buf + warp * (D + 4);
+#pragma unroll
+            for (int j = 0; j < C::NJ; ++j) {
+                float a = acc[j][0] + acc[j][1];
+                float b = acc[j][2] + acc[j][3];
+                a += __shfl_xor_sync(0xffffffffu, a, 1);
+                b += __shfl_xor_sync(0xffffffffu, b, 1);
+                a += __shfl_xor_sync(0xffffffffu, a, 2);
+                b += __shfl_xor_sync(0xffffffffu, b, 2);
+                if (c == (j & 3)) {
+                    if constexpr (D == 128) {
+                        mine[16 * g + j] = a;
+                        mine[16 * g + 8 + j] = b;
+                    } else {
+                        mine[8 * g + j] = a;
+                        mine[8 * g + 4 + j] = b;
+                    }
+                }
+            }
+            float zt = zsum;
+            zt += __shfl_xor_sync(0xffffffffu, zt, 4);
+            zt += __shfl_xor_sync(0xffffffffu, zt, 8);
+            zt += __shfl_xor_sync(0xffffffffu, zt, 16);
+            if (lane == 0) {
+                mine[D] = m2;
+                mine[D + 1] = zt;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&red_bar[par]);
+            if (!mbar_wait_bounded(&red_bar[par], red_phase[par], abort_flag, kWaitLimitNs)) {
+                *abort_flag = 1;
+                if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+                return;
+            }
+            red_phase[par] ^= 1u;
+            float* dst = partials + (uint64_t)meta.slot * (D + 4);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < C::NC; ++w) mx = fmaxf(mx, buf[w * (D + 4) + D]);
+            for (int d = threadIdx.x; d < D + 1; d += C::NC * 32) {
+                float sum = 0.f;
+#pragma unroll
+                for (int w = 0; w < C::NC; ++w) {
+                    const float mw = buf[w * (D + 4) + D];
+                    const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+                    sum += (d < D ? buf[w * (D + 4) + d] : buf[w * (D + 4) + D + 1]) * f;
+                }
+                if (d < D) dst[d] = sum;
+                else {
+                    dst[D] = mx;
+                    dst[D + 1] = sum;
+                }
+            }
+            ++seg_count;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- combine
+
+struct CombineArgs {
+    const unsigned char* ws;
+    WsLayout l;
+    const void* q;
+    const float* sk;
+    const float* sv;
+    float scale_log2;
+    void* out;
+    uint32_t rows;
+};
+
+template <typename T>
+__device__ __forceinline__ float ldq(const T* p, uint64_t i);
+template <>
+__device__ __forceinline__ float ldq<float>(const float* p, uint64_t i) {
+    return p[i];
+}
+template <>
+__device__ __forceinline__ float ldq<__nv_bfloat16>(const __nv_bfloat16* p, uint64_t i) {
+    return __bfloat162float(p[i]);
+}
+
+template <typename O>
+__device__ __forceinline__ void st_out(O* p, uint64_t i, float v);
+template <>
+__device__ __forceinline__ void st_out<float>(float* p, uint64_t i, float v) {
+    p[i] = v;
+}
+template <>
+__device__ __forceinline__ void st_out<__nv_bfloat16>(__nv_bfloat16* p, uint64_t i, float v) {
+    p[i] = __float2bfloat16_rn(v);
+}
+
+// One warp per row; lane l owns channels [l*E, l*E+E), E = D/32.
+template <int D, typename QT, typename OT>
+__global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
+    pdl_wait_primary();
+    constexpr int E = D / 32;
+    const int lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= a.rows) return;
+    const uint32_t* row_len = reinterpret_cast<const uint32_t*>(a.ws + a.l.row_len);
+    const uint32_t* row_seg = reinterpret_cast<const uint32_t*>(a.ws + a.l.row_seg);
+    const float* partials = reinterpret_cast<const float*>(a.ws + a.l.partials);
+    OT* out = reinterpret_cast<OT*>(a.out) + (uint64_t)r * D;
+    if (row_len[r] == kInvalidRow) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, __uint_as_float(0x7fc00000u));
+        return;
+    }
+    const uint32_t s0 = row_seg[r], s1 = row_seg[r + 1];
+    float mx = -INFINITY;
+    for (uint32_t s = s0; s < s1; ++s) mx = fmaxf(mx, partials[(uint64_t)s * (D + 4) + D]);
+    float ms = -INFINITY;
+    if (a.sk) {
+        const QT* q = reinterpret_cast<const QT*>(a.q) + (uint64_t)r * D;
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dot += (ldq<QT>(q, lane * E + e) * a.scale_log2) * a.sk[(uint64_t)r * D + lane * E + e];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        ms = dot;
+        mx = fmaxf(mx, ms);
+    }
+    float acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    float z = 0.f;
+    for (uint32_t s = s0; s < s1; ++s) {
+        const float* p = partials + (uint64_t)s * (D + 4);
+        const float m = p[D];
+        const float f = m == -INFINITY ? 0.f : fast_exp2(m - mx);
+        z += p[D + 1] * f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += p[lane * E + e] * f;
+    }
+    if (a.sk) {
+        const float f = fast_exp2(ms - mx);
+        z += f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += a.sv[(uint64_t)r * D + lane * E + e] * f;
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, z > 0.f ? acc[e] / z : __uint_as_float(0x7fc00000u));
+}
+
+template <int D, typename QT>
+cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
+    using C = Cfg<D>;
+    AttnArgs args{};
+    args.q = L.q;
+    args.ws = L.ws;
+    args.partials = reinterpret_cast<float*>(L.ws + L.layout.partials);
+    args.l = L.layout;
+    args.capacity = L.arena.capacity;
+    args.ks_mis = L.ks_mis;
+    args.vs_mis = L.vs_mis;
+    args.scale_log2 = L.scale_log2;
+    args.status = L.status;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(L.max_ctas);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = L.use_pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT>, L.map_k, L.map_v, L.map_ks, L.map_vs, args);
+}
+
+template <int D, typename QT, typename OT>
+cudaError_t launch_combine_t(const AttnLaunch& L, cudaStream_t stream) {
+    CombineArgs a{};
+    a.ws = L.ws;
+    a.l = L.layout;
+    a.q = L.q;
+    a.sk = L.scratch_k;
+    a.sv = L.scratch_v;
+    a.scale_log2 = L.scale_log2;
+    a.out = L.out;
+    a.rows = L.arena.rows;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((L.arena.rows + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = L.use_pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, combine_kernel<D, QT, OT>, a);
+}
+
+}  // namespace
+
+cudaError_t configure_attention_kernels(int /*device*/) {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(attn_kernel<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg<128>::SMEM_BYTES)) != cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(attn_kernel<128, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg<128>::SMEM_BYTES)) != cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(attn_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg<64>::SMEM_BYTES)) != cudaSuccess)
+        return e;
+    return cudaFuncSetAttribute(attn_kernel<64, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Cfg<64>::SMEM_BYTES);
+}
+
+uint32_t attention_scale_box_elems() { return Cfg<128>::SC_BOX; }
+
+cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
+    PlanArgs a{};
+    a.lengths = L.lengths;
+    a.ws = L.ws;
+    a.l = L.layout;
+    a.rows = L.arena.rows;
+    a.heads = L.arena.heads;
+    a.capacity = L.arena.capacity;
+    a.split = L.split;
+    a.scratch = L.scratch_k ? 1u : 0u;
+    a.max_ctas = L.max_ctas;
+    a.min_tokens = 32;
+    a.status = L.status;
+    plan_kernel<<<1, 1024, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream) {
+    const bool bq = L.q_dtype == PP_DTYPE_BF16;
+    if (L.arena.head_dim == 128) return bq ? launch_attn_t<128, __nv_bfloat16>(L, stream) : launch_attn_t<128, float>(L, stream);
+    return bq ? launch_attn_t<64, __nv_bfloat16>(L, stream) : launch_attn_t<64, float>(L, stream);
+}
+
+cudaError_t launch_combine(const AttnLaunch& L, cudaStream_t stream) {
+    const bool bq = L.q_dtype == PP_DTYPE_BF16, bo = L.out_dtype == PP_DTYPE_BF16;
+    if (L.arena.head_dim == 128) {
+        if (bq) return bo ? launch_combine_t<128, __nv_bfloat16, __nv_bfloat16>(L, stream)
+                          : launch_combine_t<128, __nv_bfloat16, float>(L, stream);
+        return bo ? launch_combine_t<128, float, __nv_bfloat16>(L, stream) : launch_combine_t<128, float, float>(L, stream);
+    }
+    if (bq) return bo ? launch_combine_t<64, __nv_bfloat16, __nv_bfloat16>(L, stream)
+                      : launch_combine_t<64, __nv_bfloat16, float>(L, stream);
+    return bo ? launch_combine_t<64, float, __nv_bfloat16>(L, stream) : launch_combine_t<64, float, float>(L, stream);
+}
+
+}  // namespace pp

@@ -1,0 +1,129 @@
+"""Deterministic input cases shared by the golden-vector generator
+(make_golden.py, run on a B200 against the reference's own kernels) and the
+tests that check the oracle and the CUDA path against those vectors.
+
+The closed-form fixtures restate the reference's own test/self-check inputs:
+  prep1      app/src/model/int8_kv_ops.rs:59-73   (sin(i*0.17)*2, past [2,1], split 32)
+  prep2      app/src/model/int8_kv_ops.rs:75-101  (rows 4, capacity 67, heads 2, view offset 1,
+                                                   past [0,66], splits {32,128})
+  cache_*    app/src/model/int8_cache.rs:19-23    (sin(i*0.173)*2 + bias)
+  hip_bf16   app/native/aten_hip/cpp/kv_int8.cpp:168-176 (bf16 K/V, B=2, H=2, C=257)
+Random cases use numpy PCG64 streams from fixed seeds.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+
+def sha(*arrays: np.ndarray) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def f32(x) -> np.ndarray:
+    return np.asarray(x, dtype=np.float32)
+
+
+def prep1() -> dict:
+    i = np.arange(384, dtype=np.float32)
+    x = (np.sin(i * np.float32(0.17)) * np.float32(2.0)).astype(np.float32).reshape(2, 3, 64)
+    j = np.arange(128, dtype=np.float32)
+    q = np.cos(j * np.float32(0.07)).astype(np.float32).reshape(2, 64)
+    sk = np.sin(j * np.float32(0.09)).astype(np.float32).reshape(2, 64)
+    return dict(x=x, q=q, sk=sk, past=np.array([2, 1], dtype=np.uint32), heads=1, split=32)
+
+
+def prep2() -> dict:
+    rows, cap, heads = 4, 67, 2
+    n = (rows + 1) * cap * 64
+    i = np.arange(n, dtype=np.float32)
+    hist = (np.sin(i * np.float32(0.013)) * np.float32(1.7)).astype(np.float32).reshape(rows + 1, cap, 64)
+    vals = (np.cos(i * np.float32(0.019)) * np.float32(0.8)).astype(np.float32).reshape(rows + 1, cap, 64)
+
+    def vec(factor, phase):
+        j = np.arange((rows + 1) * 64, dtype=np.float32)
+        return np.sin(j * np.float32(factor) + np.float32(phase)).astype(np.float32).reshape(rows + 1, 64)
+
+    return dict(hist=hist, vals=vals, q=vec(0.027, 0.4), sk=vec(0.031, 1.1), sv=vec(0.047, -0.8),
+                past_all=np.array([999, 0, 66], dtype=np.uint32), rows=rows, cap=cap, heads=heads)
+
+
+def cache_data(heads: int, count: int, bias: float) -> np.ndarray:
+    i = np.arange(heads * count * 64, dtype=np.float32)
+    return (np.sin(i * np.float32(0.173)) * np.float32(2.0) + np.float32(bias)).astype(np.float32).reshape(
+        heads, count, 64)
+
+
+CACHE_CASES = [(2, 3, 0.0), (2, 3, 1.0), (2, 1, -5.0), (2, 63, 0.0), (2, 2, 4.0), (2, 2, 7.0), (2, 1, -99.0)] + [
+    (2, 1, field * 5.0) for field in range(9)]
+
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFFFFFF
+    return (u >> 16).astype(np.uint16)
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def hip_bf16() -> dict:
+    B, H, Cn = 2, 2, 257
+    i = np.arange(B * H * Cn * 64, dtype=np.float32)
+    k = to_bf16_bits(np.sin(i * np.float32(0.013))).reshape(B, H, Cn, 64)
+    v = to_bf16_bits(np.cos(i * np.float32(0.019))).reshape(B, H, Cn, 64)
+    return dict(k_bits=k, v_bits=v)
+
+
+def edge_rows() -> np.ndarray:
+    """Rows exercising the scale floor, exact ties, clamping and extremes."""
+    rows = []
+    rows.append(np.zeros(64, np.float32))                          # scale floor 1e-12, all zero codes
+    rows.append(np.full(64, 1e-11, np.float32))                    # below the floor: s = 1e-12
+    t = np.zeros(64, np.float32)
+    t[0] = 127.0                                                   # s = 1 exactly
+    t[1:9] = [2.5, 3.5, -2.5, -3.5, 0.5, -0.5, 126.5, -126.5]      # exact ties -> half to even
+    rows.append(t)
+    rows.append(np.linspace(-1e30, 1e30, 64, dtype=np.float32))    # huge magnitudes
+    rows.append(np.linspace(-3e-38, 3e-38, 64, dtype=np.float32))  # subnormal/tiny range
+    r = np.random.Generator(np.random.PCG64(7)).standard_normal(64, dtype=np.float32)
+    r[5] = -np.abs(r).max() * 2                                    # negative extreme -> -127
+    rows.append(r)
+    rows.append(np.full(64, -4.0, np.float32))                     # constant negative row
+    return np.stack(rows).astype(np.float32)
+
+
+# Random reference-mode cases (head_dim 64, capacity <= 1024: the reference's limits).
+RANDOM_CASES = [
+    # name, seed, branches, heads, capacity, pasts (per branch), split
+    ("rand_small", 11, 3, 2, 40, [0, 17, 40], 32),
+    ("rand_ragged", 12, 4, 4, 300, [299, 1, 150, 64], 128),
+    ("rand_split1024", 13, 2, 3, 1000, [999, 500], 1024),
+    ("rand_invalid", 14, 2, 2, 64, [64, 65], 32),  # past == capacity is valid, > capacity gives NaN
+]
+
+
+def random_case(seed: int, branches: int, heads: int, cap: int) -> dict:
+    g = np.random.Generator(np.random.PCG64(seed))
+    rows = branches * heads
+    k = g.standard_normal((rows, cap, 64), dtype=np.float32)
+    v = g.standard_normal((rows, cap, 64), dtype=np.float32)
+    q = g.standard_normal((rows, 64), dtype=np.float32)
+    sk = g.standard_normal((rows, 64), dtype=np.float32)
+    sv = g.standard_normal((rows, 64), dtype=np.float32)
+    return dict(k=k, v=v, q=q, sk=sk, sv=sv)
+
+
+def cfg0_case(seed: int = 0) -> dict:
+    """batch 1, 16 heads, head_dim 64, context 1024, fp32
+    query per head, K/V from N(0,1) quantized per (token, head)."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    k = g.standard_normal((16, 1024, 64), dtype=np.float32)
+    v = g.standard_normal((16, 1024, 64), dtype=np.float32)
+    q = g.standard_normal((16, 64), dtype=np.float32)
+    return dict(k=k, v=v, q=q)

@@ -1,0 +1,247 @@
+"""Int8 decode attention on the B200 through the C ABI.
+
+Reference mode (f32 scratch token, head_dim 64) against the outputs of the
+reference's own CUDA kernels (tests/golden/ref_int8kv.npz) within the
+reference's self-check tolerance 2e-5 (int8_kv_ops.rs:73,101); history mode
+at the BASELINE shapes against the oracle within 2e-3 relative / 1e-3
+absolute, plus size-independent properties at full size."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import cases as K
+
+pytestmark = pytest.mark.gpu
+
+REF_TOL = 2e-5
+
+
+def to_dev(x, dev):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.mark.parametrize("split", [32, 128, 0])
+def test_prep1_matches_reference_kernels(pp, cuda, golden, split):
+    ops = pp.int8_kv_ops
+    c = K.prep1()
+    codes, scales = ops.quantize(to_dev(c["x"], cuda))
+    q = to_dev(c["q"], cuda).reshape(2, 1, 64)
+    sk = to_dev(c["sk"], cuda).reshape(2, 1, 64)
+    past = torch.tensor([2, 1], dtype=torch.int32, device=cuda)
+    out = ops.attention(q, codes, codes, scales, scales, sk, sk, past, 1, split)
+    np.testing.assert_allclose(host(out), golden["prep1_out"], rtol=0, atol=REF_TOL)
+
+
+@pytest.mark.parametrize("split", [32, 128, 0])
+def test_prep2_offsets_heads_splits_match_reference(pp, cuda, golden, split):
+    """Non-zero view offsets (scale arrays only 4-byte aligned), two heads per
+    sequence, an empty history and unequal lengths (int8_kv_ops.rs:75-101)."""
+    ops = pp.int8_kv_ops
+    c = K.prep2()
+    rows, heads = c["rows"], c["heads"]
+    k, ks = ops.quantize(to_dev(c["hist"], cuda)[1:].contiguous())
+    v, vs = ops.quantize(to_dev(c["vals"], cuda)[1:].contiguous())
+    kb, vb = torch.cat([k[0:1], k])[1:], torch.cat([v[0:1], v])[1:]
+    ksb, vsb = torch.cat([ks[0:1], ks])[1:], torch.cat([vs[0:1], vs])[1:]
+    assert ksb.data_ptr() % 16 != 0  # exercises the misaligned scale path
+    q = to_dev(c["q"], cuda)[1:].reshape(rows, 1, 64)
+    sk = to_dev(c["sk"], cuda)[1:].reshape(rows, 1, 64)
+    sv = to_dev(c["sv"], cuda)[1:].reshape(rows, 1, 64)
+    past = to_dev(c["past_all"].astype(np.int32), cuda)[1:]
+    out = host(ops.attention(q, kb, vb, ksb, vsb, sk, sv, past, heads, split))
+    for s in (32, 128):
+        np.testing.assert_allclose(out, golden[f"prep2_out_s{s}"], rtol=0, atol=REF_TOL)
+
+
+@pytest.mark.parametrize("case", K.RANDOM_CASES, ids=[c[0] for c in K.RANDOM_CASES])
+@pytest.mark.parametrize("split_override", [None, 0])
+def test_random_reference_mode_matches_reference_kernels(pp, cuda, golden, case, split_override):
+    name, seed, b, h, cap, pasts, split = case
+    ops = pp.int8_kv_ops
+    c = K.random_case(seed, b, h, cap)
+    assert K.sha(c["k"], c["v"], c["q"], c["sk"], c["sv"]) == str(golden[f"{name}_input_sha"])
+    rows = b * h
+    k, ks = ops.quantize(to_dev(c["k"], cuda))
+    v, vs = ops.quantize(to_dev(c["v"], cuda))
+    assert K.sha(k.cpu().numpy(), ks.cpu().numpy(), v.cpu().numpy(), vs.cpu().numpy()) == str(
+        golden[f"{name}_codes_sha"])
+    past = torch.tensor(pasts, dtype=torch.int32, device=cuda)
+    sp = split if split_override is None else split_override
+    out = host(ops.attention(to_dev(c["q"], cuda).reshape(rows, 1, 64), k, v, ks, vs,
+                             to_dev(c["sk"], cuda).reshape(rows, 1, 64), to_dev(c["sv"], cuda).reshape(rows, 1, 64),
+                             past, h, sp))
+    ref = golden[f"{name}_out"]
+    assert np.array_equal(np.isnan(out), np.isnan(ref))
+    np.testing.assert_allclose(out[~np.isnan(ref)], ref[~np.isnan(ref)], rtol=0, atol=REF_TOL)
+
+
+def test_cfg0_history_mode_matches_reference_kernels(pp, cuda, golden):
+    """BASELINE config 0 (1 branch, 16 heads, d 64, context 1024, f32 q/out)."""
+    ops = pp.int8_kv_ops
+    c = K.cfg0_case(0)
+    assert K.sha(c["k"], c["v"], c["q"]) == str(golden["cfg0_input_sha"])
+    k, ks = ops.quantize(to_dev(c["k"], cuda))
+    v, vs = ops.quantize(to_dev(c["v"], cuda))
+    assert K.sha(k.cpu().numpy(), ks.cpu().numpy(), v.cpu().numpy(), vs.cpu().numpy()) == str(golden["cfg0_codes_sha"])
+    out = ops.decode_attention(to_dev(c["q"], cuda), k, v, ks, vs, torch.tensor([1024], dtype=torch.int32, device=cuda), 16)
+    np.testing.assert_allclose(host(out), golden["cfg0_out"].reshape(16, 64), rtol=0, atol=REF_TOL)
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                                    "oracle", "_ref", "int8_kv_ref.cubin")),
+                    reason="reference kernels were not built (no reference tree when this checkout was built)")
+@pytest.mark.parametrize("seed", [31, 32])
+def test_live_against_reference_kernels(pp, cuda, seed):
+    """Same inputs through the reference's kernels and ours, in one process."""
+    from ref_runner import RefInt8Kernels
+
+    ref = RefInt8Kernels()
+    g = np.random.Generator(np.random.PCG64(seed))
+    b, h, cap = 5, 3, int(g.integers(100, 1025))
+    rows = b * h
+    kx = to_dev(g.standard_normal((rows, cap, 64), dtype=np.float32) * 2, cuda)
+    vx = to_dev(g.standard_normal((rows, cap, 64), dtype=np.float32), cuda)
+    k, ks = ref.quantize(kx)
+    v, vs = ref.quantize(vx)
+    k2, ks2 = pp.int8_kv_ops.quantize(kx)
+    assert torch.equal(k, k2) and torch.equal(ks, ks2)
+    q = to_dev(g.standard_normal((rows, 1, 64), dtype=np.float32), cuda)
+    sk = to_dev(g.standard_normal((rows, 1, 64), dtype=np.float32), cuda)
+    sv = to_dev(g.standard_normal((rows, 1, 64), dtype=np.float32), cuda)
+    pasts = torch.tensor(g.integers(0, cap + 1, b), dtype=torch.int32, device=cuda)
+    for split in (32, 128, 512):
+        want = ref.attention(q, k, v, ks, vs, sk, sv, pasts, h, split)
+        got = pp.int8_kv_ops.attention(q, k, v, ks, vs, sk, sv, pasts, h, split)
+        np.testing.assert_allclose(host(got), host(want), rtol=0, atol=REF_TOL)
+
+
+def _random_arena(pp, branches, heads, d, cap, dev, seed, dist="normal"):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    rows = branches * heads
+    if dist == "student_t":
+        # Student-t(3) * 0.7 with 1% of channels scaled by 8
+        def draw():
+            z = torch.randn(rows, cap, d, device=dev, generator=g)
+            chi = torch.randn(rows, cap, d, 3, device=dev, generator=g).pow(2).sum(-1)
+            t = z / torch.sqrt(chi / 3) * 0.7
+            mask = torch.rand(d, device=dev, generator=g) < 0.01
+            mask[int(torch.randint(0, d, (1,), device=dev, generator=g))] = True
+            return torch.where(mask, t * 8, t)
+    else:
+        def draw():
+            return torch.randn(rows, cap, d, device=dev, generator=g)
+    ops = pp.int8_kv_ops
+    k, ks = ops.quantize(draw())
+    v, vs = ops.quantize(draw())
+    return k, v, ks, vs, g
+
+
+def _oracle_rows(oracle, q, k, v, ks, vs, lens, heads, pick, sk=None, sv=None):
+    idx = torch.as_tensor(pick, device=k.device)
+    sub = lambda t: t[idx].cpu().numpy()  # noqa: E731
+    lk = np.asarray(lens)[np.asarray(pick) // heads]
+    return oracle.attention(host(q[idx]), sub(k), sub(v), sub(ks), sub(vs), lk, 1,
+                            sk=None if sk is None else host(sk[idx]), sv=None if sv is None else host(sv[idx]))
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("qdt,odt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                     (torch.bfloat16, torch.float32)])
+@pytest.mark.parametrize("split", [0, 48, 1000])
+def test_history_mode_ragged_vs_oracle(pp, oracle, cuda, d, qdt, odt, split):
+    branches, heads, cap = 6, 4, 700
+    k, v, ks, vs, g = _random_arena(pp, branches, heads, d, cap, cuda, 7 + d)
+    lens = [1, 700, 333, 16, 17, 650]
+    q = torch.randn(branches * heads, d, device=cuda, generator=g).to(qdt)
+    out = pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, torch.tensor(lens, dtype=torch.int32, device=cuda), heads,
+                                          out_dtype=odt, split_tokens=split)
+    assert out.dtype == odt
+    ref = _oracle_rows(oracle, q, k, v, ks, vs, lens, heads, list(range(branches * heads)))
+    np.testing.assert_allclose(host(out), ref, rtol=2e-3, atol=1e-3)
+    if odt == torch.float32:  # f32 output: far inside the tolerance
+        np.testing.assert_allclose(host(out), ref, rtol=0, atol=2e-5)
+
+
+def test_invalid_lengths_give_nan_rows_and_status(pp, cuda):
+    k, v, ks, vs, g = _random_arena(pp, 3, 2, 128, 64, cuda, 3)
+    q = torch.randn(6, 128, device=cuda, generator=g)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, torch.tensor([0, 65, 64], dtype=torch.int32, device=cuda),
+                                          2, status=status)
+    o = host(out)
+    assert np.isnan(o[:4]).all() and np.isfinite(o[4:]).all()
+    assert int(status.item()) & pp._native.DEV_LENGTH_RANGE
+
+
+def test_plan_reuse_across_layers(pp, oracle, cuda):
+    """One ragged plan serves all layers of a step (DecodeMetadataCache reuse)."""
+    ops = pp.int8_kv_ops
+    branches, heads, d, cap, layers = 4, 4, 128, 300, 3
+    lens = torch.tensor([300, 1, 77, 150], dtype=torch.int32, device=cuda)
+    arenas = [_random_arena(pp, branches, heads, d, cap, cuda, 40 + i) for i in range(layers)]
+    k0, v0, ks0, vs0, _ = arenas[0]
+    arena = ops.arena_struct(k0, v0, ks0, vs0, heads)
+    params = ops.attn_params(q_dtype=torch.bfloat16, out_dtype=torch.float32)
+    ws = ops.new_workspace(arena, params, cuda)
+    import ctypes as C
+    pp._native.check(pp._native.lib.pp_b200_plan_ragged(C.byref(arena), C.byref(params), ops._ptr(lens), 0,
+                                                         ops._ptr(ws), ws.numel(), ops._stream(lens)))
+    for i, (k, v, ks, vs, g) in enumerate(arenas):
+        q = torch.randn(branches * heads, d, device=cuda, generator=g).to(torch.bfloat16)
+        out = ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32, workspace=ws,
+                                   plan_ready=True)
+        ref = _oracle_rows(oracle, q, k, v, ks, vs, lens.cpu().numpy(), heads, list(range(branches * heads)))
+        np.testing.assert_allclose(host(out), ref, rtol=0, atol=2e-5)
+
+
+def test_prepare_self_check_passes(pp, cuda):
+    pp.int8_kv_ops.prepare(cuda)
+
+
+def test_cfg1_full_size(pp, oracle, cuda):
+    """BASELINE config 1 at full size: 32 branches x 16 heads, d 128, context
+    4096, bf16 q and out.  Sampled rows against the oracle; all rows finite;
+    split invariance between the automatic plan and fixed 128-token splits."""
+    branches, heads, d, L = 32, 16, 128, 4096
+    k, v, ks, vs, g = _random_arena(pp, branches, heads, d, L, cuda, 1)
+    q = torch.randn(branches * heads, d, device=cuda, generator=g).to(torch.bfloat16)
+    lens = torch.full((branches,), L, dtype=torch.int32, device=cuda)
+    out = pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.bfloat16)
+    assert torch.isfinite(out.float()).all()
+    pick = [0, 1, 15, 16, 200, 257, 400, 511]
+    ref = _oracle_rows(oracle, q, k, v, ks, vs, lens.cpu().numpy(), heads, pick)
+    np.testing.assert_allclose(host(out)[pick], ref, rtol=2e-3, atol=1e-3)
+    out32 = pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32)
+    fixed = pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32, split_tokens=128)
+    np.testing.assert_allclose(host(out32), host(fixed), rtol=0, atol=1e-5)
+    np.testing.assert_allclose(host(out32)[pick], ref, rtol=0, atol=2e-5)
+
+
+def test_cfg4_long_context_split_sweep(pp, oracle, cuda):
+    """8 branches x 16 heads, d 128, context 16384,
+    heavy-tailed K/V with outlier channels; split factors 4, 8, 16, 32."""
+    branches, heads, d, L = 8, 16, 128, 16384
+    k, v, ks, vs, g = _random_arena(pp, branches, heads, d, L, cuda, 4, dist="student_t")
+    q = torch.randn(branches * heads, d, device=cuda, generator=g).to(torch.bfloat16)
+    lens = torch.full((branches,), L, dtype=torch.int32, device=cuda)
+    outs = {}
+    for splits in (4, 8, 16, 32):
+        outs[splits] = host(pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32,
+                                                           split_tokens=L // splits))
+    outs[0] = host(pp.int8_kv_ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32))
+    for s, o in outs.items():
+        assert np.isfinite(o).all()
+        np.testing.assert_allclose(o, outs[4], rtol=0, atol=2e-5)
+    pick = [0, 5, 31, 64, 127]
+    ref = _oracle_rows(oracle, q, k, v, ks, vs, lens.cpu().numpy(), heads, pick)
+    np.testing.assert_allclose(outs[32][pick], ref, rtol=2e-3, atol=1e-3)
+    np.testing.assert_allclose(outs[32][pick], ref, rtol=0, atol=5e-5)
