@@ -18,6 +18,7 @@
 
 namespace pp {
 uint32_t attention_scale_box_elems();
+uint32_t attention_stage_tokens();
 }
 
 namespace {
@@ -133,11 +134,12 @@ uint32_t ctas_for(const PpAttnParams& p, const DeviceInfo& d) {
 }
 
 // 2-D map over the packed codes: dims {head_dim, rows*capacity} bytes, boxes of
-// 16 tokens, swizzled so the consumer warps read shared memory conflict-free.
-int32_t encode_codes_map(CUtensorMap* map, const uint8_t* base, const PpKvArena& a) {
+// `box_tokens` tokens, swizzled so the consumer warps read shared memory
+// without bank conflicts.
+int32_t encode_codes_map(CUtensorMap* map, const uint8_t* base, const PpKvArena& a, uint32_t box_tokens) {
     cuuint64_t dims[2] = {a.head_dim, (cuuint64_t)a.rows * a.capacity};
     cuuint64_t strides[1] = {a.head_dim};
-    cuuint32_t box[2] = {a.head_dim, 16};
+    cuuint32_t box[2] = {a.head_dim, box_tokens};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -314,8 +316,11 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     L.q = q;
     L.out = out;
     L.status = status;
-    if ((s = encode_codes_map(&L.map_k, arena->k, *arena))) return s;
-    if ((s = encode_codes_map(&L.map_v, arena->v, *arena))) return s;
+    const uint32_t stage = pp::attention_stage_tokens();
+    if ((s = encode_codes_map(&L.map_k, arena->k, *arena, 16))) return s;
+    if ((s = encode_codes_map(&L.map_v, arena->v, *arena, 16))) return s;
+    if ((s = encode_codes_map(&L.map_k_stage, arena->k, *arena, stage))) return s;
+    if ((s = encode_codes_map(&L.map_v_stage, arena->v, *arena, stage))) return s;
     if ((s = encode_scale_map(&L.map_ks, &L.ks_mis, arena->k_scale, *arena))) return s;
     if ((s = encode_scale_map(&L.map_vs, &L.vs_mis, arena->v_scale, *arena))) return s;
     cudaStream_t st = (cudaStream_t)stream;

@@ -90,8 +90,9 @@ struct AttnLaunch {
     uint32_t* status;
     bool plan_ready;
     bool use_pdl;
-    // Tensor maps (host-encoded) for K, V codes and K, V scales.
-    CUtensorMap map_k, map_v, map_ks, map_vs;
+    // Tensor maps (host-encoded): K, V codes in 16-token boxes and in
+    // whole-stage boxes, and K, V scales.
+    CUtensorMap map_k, map_v, map_k_stage, map_v_stage, map_ks, map_vs;
     uint32_t ks_mis, vs_mis;  // element offset of the scale arrays inside their maps
 };
 

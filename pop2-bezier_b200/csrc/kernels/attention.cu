@@ -18,6 +18,8 @@
 //   * combine_kernel merges the per-segment partials (and, in reference mode,
 //     the scratch token) with a log-sum-exp combine.
 // All softmax arithmetic runs in base 2 (scores pre-scaled by log2 e).
+#include <type_traits>
+
 #include "common.cuh"
 #include "../host/internal.h"
 
@@ -25,6 +27,7 @@ namespace pp {
 namespace {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: generous, never hit in normal runs
+constexpr float kSlack = 8.0f;  // log2-domain headroom before the softmax reference point moves
 
 // ------------------------------------------------------------------ plan
 
@@ -176,9 +179,21 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
 
 // ------------------------------------------------------------- attention
 
+// Consumer warps per CTA and ring depth (tuning knobs; the defaults were
+// chosen by measurement on B200).
+#ifndef PP_ATTN_NC
+#define PP_ATTN_NC 12
+#endif
+#ifndef PP_ATTN_STAGES_D128
+#define PP_ATTN_STAGES_D128 4
+#endif
+#ifndef PP_ATTN_STAGES_D64
+#define PP_ATTN_STAGES_D64 7
+#endif
+
 template <int D>
 struct Cfg {
-    static constexpr int NC = 8;                    // consumer warps
+    static constexpr int NC = PP_ATTN_NC;           // consumer warps
     static constexpr int THREADS = (NC + 1) * 32;   // + one producer warp
     static constexpr int BOX = 16;                  // tokens per TMA box = one consumer warp's slice
     static constexpr int T = BOX * NC;              // tokens per stage
@@ -194,7 +209,8 @@ struct Cfg {
     static constexpr int OFF_Q = OFF_VS + SC_SLOT;
     static constexpr int OFF_META = OFF_Q + Q_BYTES;
     static constexpr int STAGE_BYTES = ((OFF_META + 32 + 1023) / 1024) * 1024;
-    static constexpr int STAGES = D == 128 ? 5 : 8;
+    static constexpr int STAGES = D == 128 ? PP_ATTN_STAGES_D128 : PP_ATTN_STAGES_D64;
+    static_assert(T <= 256, "a whole-stage TMA box holds at most 256 tokens");
     static constexpr int RED_FLOATS = NC * (D + 4);
     static constexpr int OFF_RED = STAGES * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_RED + 2 * RED_FLOATS * 4;
@@ -260,6 +276,7 @@ __device__ __forceinline__ uint32_t split_term_pack(float a, float b, int part) 
 template <int D, typename QT>
 __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                const __grid_constant__ CUtensorMap map_k_stage, const __grid_constant__ CUtensorMap map_v_stage,
                 const __grid_constant__ CUtensorMap map_ks, const __grid_constant__ CUtensorMap map_vs,
                 const AttnArgs args) {
     using C = Cfg<D>;
@@ -285,6 +302,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     if (warp == C::NC && lane == 0) {
         tma_prefetch_desc(&map_k);
         tma_prefetch_desc(&map_v);
+        tma_prefetch_desc(&map_k_stage);
+        tma_prefetch_desc(&map_v_stage);
         tma_prefetch_desc(&map_ks);
         tma_prefetch_desc(&map_vs);
     }
@@ -334,9 +353,14 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 meta->vs_off = args.vs_mis + tok - vsx;
                 const uint32_t bytes = nbox * C::BOX * D * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                for (uint32_t b = 0; b < nbox; ++b) {
-                    tma_load_2d(st + C::OFF_K + b * C::BOX * D, &map_k, &full[slot], 0, (int32_t)(tok + b * C::BOX));
-                    tma_load_2d(st + C::OFF_V + b * C::BOX * D, &map_v, &full[slot], 0, (int32_t)(tok + b * C::BOX));
+                if (n == (uint32_t)C::T) {  // full stage: one box of T tokens each for K and V
+                    tma_load_2d(st + C::OFF_K, &map_k_stage, &full[slot], 0, (int32_t)tok);
+                    tma_load_2d(st + C::OFF_V, &map_v_stage, &full[slot], 0, (int32_t)tok);
+                } else {  // segment tail: 16-token boxes, none wholly past the segment
+                    for (uint32_t b = 0; b < nbox; ++b) {
+                        tma_load_2d(st + C::OFF_K + b * C::BOX * D, &map_k, &full[slot], 0, (int32_t)(tok + b * C::BOX));
+                        tma_load_2d(st + C::OFF_V + b * C::BOX * D, &map_v, &full[slot], 0, (int32_t)(tok + b * C::BOX));
+                    }
                 }
                 tma_load_1d(st + C::OFF_KS, &map_ks, &full[slot], (int32_t)ksx);
                 tma_load_1d(st + C::OFF_VS, &map_vs, &full[slot], (int32_t)vsx);
@@ -375,7 +399,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     for (int j = 0; j < C::NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 #pragma unroll
     for (int i = 0; i < C::NI; ++i) qb[i][0] = qb[i][1] = 0u;
-    uint32_t red_phase[2] = {0u, 0u};
+    uint32_t red_phase_bits = 0u;  // bit p: parity to wait for on red_bar[p]
     uint32_t seg_count = 0;
     float* partials = args.partials;
 
@@ -387,10 +411,14 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             return;
         }
         unsigned char* st = smem + slot * C::STAGE_BYTES;
-        const StageMeta meta = *reinterpret_cast<const StageMeta*>(st + C::OFF_META);
-        if (meta.flags & kTerm) break;
+        // StageMeta {row, t, nvalid, slot | flags, ks_off, vs_off, pad}
+        const uint4 m0 = lds128(smem_addr(st + C::OFF_META));
+        const uint4 m1 = lds128(smem_addr(st + C::OFF_META) + 16u);
+        const uint32_t flags = m1.x;
+        if (flags & kTerm) break;
+        const uint32_t nvalid = m0.z, seg_slot = m0.w, ks_off = m1.y, vs_off = m1.z;
 
-        if (meta.flags & kFirst) {
+        if (flags & kFirst) {
             // q row -> three-term bf16 B fragments for channel slice of thread c.
             constexpr int QN = D / 4;  // channels per thread: [QN*c, QN*c + QN)
             float qv[QN];
@@ -409,66 +437,80 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
 
         const int tok0 = warp * C::BOX;
-        const int nv = (int)meta.nvalid - tok0;
-        if (nv > 0) {
+        const int nv = (int)nvalid - tok0;
+        // One 16-token block of this warp.  MASKED handles a segment's ragged
+        // last block (tokens >= nv contribute nothing); full blocks skip masking.
+        auto block = [&](auto masked_tag) {
+            constexpr bool MASKED = decltype(masked_tag)::value;
             const uint32_t kt = smem_addr(st + C::OFF_K + tok0 * D);
             const uint32_t vt = smem_addr(st + C::OFF_V + tok0 * D);
-            const uint32_t ks = smem_addr(st + C::OFF_KS) + (meta.ks_off + tok0) * 4u;
-            const uint32_t vs = smem_addr(st + C::OFF_VS) + (meta.vs_off + tok0) * 4u;
+            const uint32_t ks = smem_addr(st + C::OFF_KS) + (ks_off + tok0) * 4u;
+            const uint32_t vs = smem_addr(st + C::OFF_VS) + (vs_off + tok0) * 4u;
+            auto scale = [&](uint32_t addr, int e) -> float {
+                if constexpr (MASKED) return e < nv ? lds_f32(addr + e * 4) : 0.f;
+                else return lds_f32(addr + e * 4);
+            };
 
             // ---- scores: q . k for tokens g and g+8 of this warp's box
-            const float sg = g < nv ? lds_f32(ks + g * 4) : 0.f;
-            const float sg8 = g + 8 < nv ? lds_f32(ks + (g + 8) * 4) : 0.f;
-            float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+            const float sg = scale(ks, g), sg8 = scale(ks, g + 8);
+            const uint64_t sg2 = f2_pack(sg, sg), sg82 = f2_pack(sg8, sg8);
+            float sacc[4] = {0.f, 0.f, 0.f, 0.f}, sacc2[4] = {0.f, 0.f, 0.f, 0.f};
+            // k_t = bf16(i8 * ks[t]) for 4 channels of token g (a) and g+8 (b),
+            // accumulated against the q fragments of MMA i
+            auto qk_mma = [&](int i, uint32_t wa, uint32_t wb) {
+                uint64_t a01, a23, b01, b23;
+                i8x4_to_f32x2(wa, a01, a23);
+                i8x4_to_f32x2(wb, b01, b23);
+                a01 = f2_mul(a01, sg2);
+                a23 = f2_mul(a23, sg2);
+                b01 = f2_mul(b01, sg82);
+                b23 = f2_mul(b23, sg82);
+                // two independent accumulator chains halve the MMA dependency depth
+                mma_bf16_16816((i & 1) ? sacc2 : sacc, pack_bf16x2_f2(a01), pack_bf16x2_f2(b01),
+                               pack_bf16x2_f2(a23), pack_bf16x2_f2(b23), qb[i][0], qb[i][1]);
+            };
             if constexpr (D == 128) {
                 // 128B swizzle: row e, 16B chunk x stored at chunk x ^ (e & 7).
                 const uint4 ka0 = lds128(kt + g * 128 + (((2 * c) ^ g) << 4));
                 const uint4 ka1 = lds128(kt + g * 128 + (((2 * c + 1) ^ g) << 4));
                 const uint4 kb0 = lds128(kt + (g + 8) * 128 + (((2 * c) ^ g) << 4));
                 const uint4 kb1 = lds128(kt + (g + 8) * 128 + (((2 * c + 1) ^ g) << 4));
-                const uint32_t wa[8] = {ka0.x, ka0.y, ka0.z, ka0.w, ka1.x, ka1.y, ka1.z, ka1.w};
-                const uint32_t wb[8] = {kb0.x, kb0.y, kb0.z, kb0.w, kb1.x, kb1.y, kb1.z, kb1.w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    float a0, a1, a2, a3, b0, b1, b2, b3;
-                    i8x4_to_f32(wa[i], a0, a1, a2, a3);
-                    i8x4_to_f32(wb[i], b0, b1, b2, b3);
-                    mma_bf16_16816(sacc, pack_bf16x2(a0 * sg, a1 * sg), pack_bf16x2(b0 * sg8, b1 * sg8),
-                                   pack_bf16x2(a2 * sg, a3 * sg), pack_bf16x2(b2 * sg8, b3 * sg8), qb[i][0],
-                                   qb[i][1]);
-                }
+                qk_mma(0, ka0.x, kb0.x);
+                qk_mma(1, ka0.y, kb0.y);
+                qk_mma(2, ka0.z, kb0.z);
+                qk_mma(3, ka0.w, kb0.w);
+                qk_mma(4, ka1.x, kb1.x);
+                qk_mma(5, ka1.y, kb1.y);
+                qk_mma(6, ka1.z, kb1.z);
+                qk_mma(7, ka1.w, kb1.w);
             } else {
                 // 64B swizzle: row e, 16B chunk x stored at chunk x ^ ((e >> 1) & 3).
                 const int sw = (g >> 1) & 3;
                 const uint4 ka = lds128(kt + g * 64 + ((c ^ sw) << 4));
                 const uint4 kb = lds128(kt + (g + 8) * 64 + ((c ^ sw) << 4));
-                const uint32_t wa[4] = {ka.x, ka.y, ka.z, ka.w};
-                const uint32_t wb[4] = {kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float a0, a1, a2, a3, b0, b1, b2, b3;
-                    i8x4_to_f32(wa[i], a0, a1, a2, a3);
-                    i8x4_to_f32(wb[i], b0, b1, b2, b3);
-                    mma_bf16_16816(sacc, pack_bf16x2(a0 * sg, a1 * sg), pack_bf16x2(b0 * sg8, b1 * sg8),
-                                   pack_bf16x2(a2 * sg, a3 * sg), pack_bf16x2(b2 * sg8, b3 * sg8), qb[i][0],
-                                   qb[i][1]);
-                }
+                qk_mma(0, ka.x, kb.x);
+                qk_mma(1, ka.y, kb.y);
+                qk_mma(2, ka.z, kb.z);
+                qk_mma(3, ka.w, kb.w);
             }
-            float s_g = sacc[0] + sacc[1];
-            float s_g8 = sacc[2] + sacc[3];
+            float s_g = (sacc[0] + sacc2[0]) + (sacc[1] + sacc2[1]);
+            float s_g8 = (sacc[2] + sacc2[2]) + (sacc[3] + sacc2[3]);
             s_g += __shfl_xor_sync(0xffffffffu, s_g, 1);
             s_g8 += __shfl_xor_sync(0xffffffffu, s_g8, 1);
             s_g += __shfl_xor_sync(0xffffffffu, s_g, 2);
             s_g8 += __shfl_xor_sync(0xffffffffu, s_g8, 2);
-            if (g >= nv) s_g = -INFINITY;
-            if (g + 8 >= nv) s_g8 = -INFINITY;
+            if constexpr (MASKED) {
+                if (g >= nv) s_g = -INFINITY;
+                if (g + 8 >= nv) s_g8 = -INFINITY;
+            }
 
-            // ---- online softmax (base 2)
-            float bm = fmaxf(s_g, s_g8);
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
-            if (bm > m2) {
+            // ---- online softmax (base 2) with a lazy reference point: m2 moves
+            // only when a score exceeds it by more than kSlack, so p <= 2^kSlack.
+            const float sm = fmaxf(s_g, s_g8);
+            if (__any_sync(0xffffffffu, sm > m2 + kSlack)) {
+                float bm = fmaxf(sm, __shfl_xor_sync(0xffffffffu, sm, 4));
+                bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+                bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
                 const float alpha = fast_exp2(m2 - bm);
                 zsum *= alpha;
 #pragma unroll
@@ -483,47 +525,64 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             const float p_g = fast_exp2(s_g - m2), p_g8 = fast_exp2(s_g8 - m2);
             zsum += p_g + p_g8;
 
-            // ---- p as the B operand: tokens 2c, 2c+1, 2c+8, 2c+9, term g
-            const float x0 = __shfl_sync(0xffffffffu, p_g, 8 * c);
-            const float x1 = __shfl_sync(0xffffffffu, p_g, 8 * c + 4);
-            const float x2 = __shfl_sync(0xffffffffu, p_g8, 8 * c);
-            const float x3 = __shfl_sync(0xffffffffu, p_g8, 8 * c + 4);
-            const uint32_t pb0 = split_term_pack(x0, x1, g);
-            const uint32_t pb1 = split_term_pack(x2, x3, g);
+            // ---- p as the B operand (k = tokens 2c, 2c+1, 2c+8, 2c+9; n = term g).
+            // Lane (G, c) holds term c of its tokens G and G+8; thread (g, c) pulls
+            // term g of tokens 2c, 2c+1 from the lanes of groups 2c, 2c+1.
+            uint32_t terms;
+            {
+                const uint32_t h = pack_bf16x2(p_g, p_g8);
+                const float r0 = p_g - bf16_lo_to_f32(h), r1 = p_g8 - bf16_hi_to_f32(h);
+                const uint32_t l = pack_bf16x2(r0, r1);
+                const uint32_t l2 = pack_bf16x2(r0 - bf16_lo_to_f32(l), r1 - bf16_hi_to_f32(l));
+                terms = c == 0 ? h : c == 1 ? l : c == 2 ? l2 : 0u;
+            }
+            const uint32_t tx = __shfl_sync(0xffffffffu, terms, 8 * c + (g & 3));
+            const uint32_t ty = __shfl_sync(0xffffffffu, terms, 8 * c + 4 + (g & 3));
+            const uint32_t pb0 = g < 3 ? __byte_perm(tx, ty, 0x5410) : 0u;
+            const uint32_t pb1 = g < 3 ? __byte_perm(tx, ty, 0x7632) : 0u;
 
             // ---- p . V: A = V^T (rows = channels, k = tokens 2c, 2c+1, 2c+8, 2c+9)
             const int e0 = 2 * c, e1 = 2 * c + 1, e2 = 2 * c + 8, e3 = 2 * c + 9;
-            const float v0s = e0 < nv ? lds_f32(vs + e0 * 4) : 0.f;
-            const float v1s = e1 < nv ? lds_f32(vs + e1 * 4) : 0.f;
-            const float v2s = e2 < nv ? lds_f32(vs + e2 * 4) : 0.f;
-            const float v3s = e3 < nv ? lds_f32(vs + e3 * 4) : 0.f;
+            const float v0s = scale(vs, e0), v1s = scale(vs, e1), v2s = scale(vs, e2), v3s = scale(vs, e3);
+            const uint64_t s0 = f2_pack(v0s, v0s), s1 = f2_pack(v1s, v1s);
+            const uint64_t s2 = f2_pack(v2s, v2s), s3 = f2_pack(v3s, v3s);
+            // channels x..x+3 of the four tokens (words w0..w3) -> 4 MMAs, starting
+            // at accumulator j0 (channel rows of the A tile: m = g -> word wa, m = g+8 -> word wb)
+            auto pv_mma4 = [&](int j0, uint32_t wa0, uint32_t wa1, uint32_t wa2, uint32_t wa3, uint32_t wb0,
+                               uint32_t wb1, uint32_t wb2, uint32_t wb3) {
+                uint64_t a[4][2], b[4][2];  // [token][pair]: channels (x, x+1), (x+2, x+3)
+                i8x4_to_f32x2(wa0, a[0][0], a[0][1]);
+                i8x4_to_f32x2(wa1, a[1][0], a[1][1]);
+                i8x4_to_f32x2(wa2, a[2][0], a[2][1]);
+                i8x4_to_f32x2(wa3, a[3][0], a[3][1]);
+                i8x4_to_f32x2(wb0, b[0][0], b[0][1]);
+                i8x4_to_f32x2(wb1, b[1][0], b[1][1]);
+                i8x4_to_f32x2(wb2, b[2][0], b[2][1]);
+                i8x4_to_f32x2(wb3, b[3][0], b[3][1]);
+                const uint64_t sc[4] = {s0, s1, s2, s3};
+                float fa[4][4], fb[4][4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    f2_unpack(f2_mul(a[t][0], sc[t]), fa[t][0], fa[t][1]);
+                    f2_unpack(f2_mul(a[t][1], sc[t]), fa[t][2], fa[t][3]);
+                    f2_unpack(f2_mul(b[t][0], sc[t]), fb[t][0], fb[t][1]);
+                    f2_unpack(f2_mul(b[t][1], sc[t]), fb[t][2], fb[t][3]);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    mma_bf16_16816(acc[j0 + e], pack_bf16x2(fa[0][e], fa[1][e]), pack_bf16x2(fb[0][e], fb[1][e]),
+                                   pack_bf16x2(fa[2][e], fa[3][e]), pack_bf16x2(fb[2][e], fb[3][e]), pb0, pb1);
+                }
+            };
             if constexpr (D == 128) {
                 // thread holds channels [16g, 16g+16) of its four tokens
                 const uint4 v0 = lds128(vt + e0 * 128 + ((g ^ e0) << 4));
                 const uint4 v1 = lds128(vt + e1 * 128 + ((g ^ e1) << 4));
                 const uint4 v2 = lds128(vt + e2 * 128 + ((g ^ (e2 & 7)) << 4));
                 const uint4 v3 = lds128(vt + e3 * 128 + ((g ^ (e3 & 7)) << 4));
-                const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
-                const uint32_t w2[4] = {v2.x, v2.y, v2.z, v2.w}, w3[4] = {v3.x, v3.y, v3.z, v3.w};
-#pragma unroll
-                for (int jw = 0; jw < 2; ++jw) {
-                    float a[4][4], b[4][4];  // [token][elem]: a = channels 16g+4jw+e, b = +8
-                    i8x4_to_f32(w0[jw], a[0][0], a[0][1], a[0][2], a[0][3]);
-                    i8x4_to_f32(w1[jw], a[1][0], a[1][1], a[1][2], a[1][3]);
-                    i8x4_to_f32(w2[jw], a[2][0], a[2][1], a[2][2], a[2][3]);
-                    i8x4_to_f32(w3[jw], a[3][0], a[3][1], a[3][2], a[3][3]);
-                    i8x4_to_f32(w0[2 + jw], b[0][0], b[0][1], b[0][2], b[0][3]);
-                    i8x4_to_f32(w1[2 + jw], b[1][0], b[1][1], b[1][2], b[1][3]);
-                    i8x4_to_f32(w2[2 + jw], b[2][0], b[2][1], b[2][2], b[2][3]);
-                    i8x4_to_f32(w3[2 + jw], b[3][0], b[3][1], b[3][2], b[3][3]);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        mma_bf16_16816(acc[4 * jw + e], pack_bf16x2(a[0][e] * v0s, a[1][e] * v1s),
-                                       pack_bf16x2(b[0][e] * v0s, b[1][e] * v1s),
-                                       pack_bf16x2(a[2][e] * v2s, a[3][e] * v3s),
-                                       pack_bf16x2(b[2][e] * v2s, b[3][e] * v3s), pb0, pb1);
-                    }
-                }
+                // accumulator j: channel 16g + j (m = g) and 16g + 8 + j (m = g + 8)
+                pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.z, v1.z, v2.z, v3.z);
+                pv_mma4(4, v0.y, v1.y, v2.y, v3.y, v0.w, v1.w, v2.w, v3.w);
             } else {
                 // thread holds channels [8g, 8g+8) of its four tokens
                 const uint32_t off = ((((uint32_t)g >> 1) ^ (uint32_t)c) << 4) + (((uint32_t)g & 1u) << 3);
@@ -531,28 +590,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 const uint2 v1 = lds64(vt + e1 * 64 + off);
                 const uint2 v2 = lds64(vt + e2 * 64 + off);
                 const uint2 v3 = lds64(vt + e3 * 64 + off);
-                float a[4][4], b[4][4];
-                i8x4_to_f32(v0.x, a[0][0], a[0][1], a[0][2], a[0][3]);
-                i8x4_to_f32(v1.x, a[1][0], a[1][1], a[1][2], a[1][3]);
-                i8x4_to_f32(v2.x, a[2][0], a[2][1], a[2][2], a[2][3]);
-                i8x4_to_f32(v3.x, a[3][0], a[3][1], a[3][2], a[3][3]);
-                i8x4_to_f32(v0.y, b[0][0], b[0][1], b[0][2], b[0][3]);
-                i8x4_to_f32(v1.y, b[1][0], b[1][1], b[1][2], b[1][3]);
-                i8x4_to_f32(v2.y, b[2][0], b[2][1], b[2][2], b[2][3]);
-                i8x4_to_f32(v3.y, b[3][0], b[3][1], b[3][2], b[3][3]);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    mma_bf16_16816(acc[e], pack_bf16x2(a[0][e] * v0s, a[1][e] * v1s),
-                                   pack_bf16x2(b[0][e] * v0s, b[1][e] * v1s),
-                                   pack_bf16x2(a[2][e] * v2s, a[3][e] * v3s),
-                                   pack_bf16x2(b[2][e] * v2s, b[3][e] * v3s), pb0, pb1);
-                }
+                // accumulator j: channel 8g + j (m = g) and 8g + 4 + j (m = g + 8)
+                pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.y, v1.y, v2.y, v3.y);
             }
-        }
+        };
+        if (nv >= C::BOX) block(std::false_type{});
+        else if (nv > 0) block(std::true_type{});
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
 
-        if (meta.flags & kLast) {
+        if (flags & kLast) {
             // ---- segment epilogue: merge the NC warp states into one partial
             const uint32_t par = seg_count & 1u;
             float* buf = red + par * C::RED_FLOATS;
@@ -585,13 +632,13 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_bar[par]);
-            if (!mbar_wait_bounded(&red_bar[par], red_phase[par], abort_flag, kWaitLimitNs)) {
+            if (!mbar_wait_bounded(&red_bar[par], (red_phase_bits >> par) & 1u, abort_flag, kWaitLimitNs)) {
                 *abort_flag = 1;
                 if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
                 return;
             }
-            red_phase[par] ^= 1u;
-            float* dst = partials + (uint64_t)meta.slot * (D + 4);
+            red_phase_bits ^= 1u << par;
+            float* dst = partials + (uint64_t)seg_slot * (D + 4);
             float mx = -INFINITY;
 #pragma unroll
             for (int w = 0; w < C::NC; ++w) mx = fmaxf(mx, buf[w * (D + 4) + D]);
@@ -725,7 +772,8 @@ cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = L.use_pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT>, L.map_k, L.map_v, L.map_ks, L.map_vs, args);
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT>, L.map_k, L.map_v, L.map_k_stage, L.map_v_stage, L.map_ks,
+                              L.map_vs, args);
 }
 
 template <int D, typename QT, typename OT>
@@ -770,6 +818,7 @@ cudaError_t configure_attention_kernels(int /*device*/) {
 }
 
 uint32_t attention_scale_box_elems() { return Cfg<128>::SC_BOX; }
+uint32_t attention_stage_tokens() { return Cfg<128>::T; }
 
 cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
     PlanArgs a{};

@@ -36,6 +36,52 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, fl
     f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - bias;
 }
 
+// ------------------------------------------------------- packed f32x2 (sm_100)
+// Two IEEE round-to-nearest f32 operations per instruction; results are
+// bit-identical to the scalar add/mul.
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// Exact conversion of the four signed bytes of `w` to f32 pairs (b0, b1) and
+// (b2, b3), as i8x4_to_f32 but with packed subtraction.
+__device__ __forceinline__ void i8x4_to_f32x2(uint32_t w, uint64_t& p01, uint64_t& p23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint64_t bias = f2_pack(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    p01 = f2_add(f2_pack(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                         __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541))),
+                 bias);
+    p23 = f2_add(f2_pack(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                         __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543))),
+                 bias);
+}
+
+// bf16x2 of an f32 pair (RNE), lo element in bits 0..15.
+__device__ __forceinline__ uint32_t pack_bf16x2_f2(uint64_t v) {
+    float lo, hi;
+    f2_unpack(v, lo, hi);
+    return pack_bf16x2(lo, hi);
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
