@@ -316,7 +316,7 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     L.q = q;
     L.out = out;
     L.status = status;
-    const uint32_t stage = pp::attention_stage_tokens();
+    const uint32_t stage = pp::attention_stage_tokens();  // rows of one whole-stage box
     if ((s = encode_codes_map(&L.map_k, arena->k, *arena, 16))) return s;
     if ((s = encode_codes_map(&L.map_v, arena->v, *arena, 16))) return s;
     if ((s = encode_codes_map(&L.map_k_stage, arena->k, *arena, stage))) return s;

@@ -10,11 +10,15 @@
 //     gets the same number of tokens whatever the raggedness), or into
 //     fixed-size splits when the caller asks for the reference's split_tokens.
 //   * attn_kernel is persistent, one CTA per SM: a producer warp streams
-//     16-token boxes of int8 K/V (TMA, 128B/64B swizzle) and their scales into
-//     a multi-stage shared-memory ring guarded by mbarriers; eight consumer
-//     warps dequantize to bf16 in registers and run the two dot products
-//     (q.k and p.V) on the tensor cores (mma.sync m16n8k16, f32 accumulate),
-//     with q and p split into three bf16 terms so the products are exact in f32.
+//     whole stages of int8 K/V (TMA, 128B/64B swizzle) and their scales into
+//     a multi-stage shared-memory ring guarded by mbarriers; consumer warps
+//     dequantize to bf16 in registers and run the two dot products (q.k and
+//     p.V) on the tensor cores (mma.sync m16n8k16, f32 accumulate), with q
+//     and p split into three bf16 terms so the products are exact in f32.
+//   * dequant per element: a byte permute builds the float 2^23 + 128 + i,
+//     a packed f32 add removes the bias exactly, a packed f32 multiply
+//     applies the scale (the reference's f32 product) and a bf16x2 pack
+//     rounds to nearest even, so bf16(i8 * scale) is reproduced bit for bit.
 //   * combine_kernel merges the per-segment partials (and, in reference mode,
 //     the scratch token) with a log-sum-exp combine.
 // All softmax arithmetic runs in base 2 (scores pre-scaled by log2 e).
@@ -179,27 +183,33 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
 
 // ------------------------------------------------------------- attention
 
-// Consumer warps per CTA and ring depth (tuning knobs; the defaults were
-// chosen by measurement on B200).
+// Consumer warps per CTA, 16-token MMA blocks per warp per stage, and ring
+// depth (tuning knobs; the defaults were chosen by measurement on B200).
 #ifndef PP_ATTN_NC
-#define PP_ATTN_NC 12
+#define PP_ATTN_NC 11
+#endif
+#ifndef PP_ATTN_NB
+#define PP_ATTN_NB 2
 #endif
 #ifndef PP_ATTN_STAGES_D128
-#define PP_ATTN_STAGES_D128 4
+#define PP_ATTN_STAGES_D128 2
 #endif
 #ifndef PP_ATTN_STAGES_D64
-#define PP_ATTN_STAGES_D64 7
+#define PP_ATTN_STAGES_D64 4
 #endif
 
 template <int D>
 struct Cfg {
     static constexpr int NC = PP_ATTN_NC;           // consumer warps
     static constexpr int THREADS = (NC + 1) * 32;   // + one producer warp
-    static constexpr int BOX = 16;                  // tokens per TMA box = one consumer warp's slice
-    static constexpr int T = BOX * NC;              // tokens per stage
+    static constexpr int BOX = 16;                  // tokens per MMA block and per tail TMA box
+    static constexpr int NB = PP_ATTN_NB;           // MMA blocks per consumer warp per stage
+    static constexpr int TPW = BOX * NB;            // tokens per consumer warp per stage
+    static constexpr int T = TPW * NC;              // tokens per stage
     static constexpr int KV_BYTES = T * D;
-    static constexpr int SC_BOX = T + 4;            // scale elements per stage (+ alignment slack)
-    static constexpr int SC_BYTES = SC_BOX * 4;
+    static constexpr int SC_BOX = 160;              // scale elements per TMA box (640 B: keeps every box 128B-aligned)
+    static constexpr int SC_BOXES = (T + 4 + SC_BOX - 1) / SC_BOX;  // T tokens + alignment slack
+    static constexpr int SC_BYTES = SC_BOXES * SC_BOX * 4;
     static constexpr int Q_BYTES = D * 4;
     static constexpr int OFF_K = 0;
     static constexpr int OFF_V = KV_BYTES;
@@ -210,12 +220,21 @@ struct Cfg {
     static constexpr int OFF_META = OFF_Q + Q_BYTES;
     static constexpr int STAGE_BYTES = ((OFF_META + 32 + 1023) / 1024) * 1024;
     static constexpr int STAGES = D == 128 ? PP_ATTN_STAGES_D128 : PP_ATTN_STAGES_D64;
-    static_assert(T <= 256, "a whole-stage TMA box holds at most 256 tokens");
+    static constexpr int STAGE_BOXES = (T + 255) / 256;  // TMA boxes hold at most 256 rows
+    static constexpr int STAGE_BOX = T / STAGE_BOXES;    // tokens per whole-stage box
+    static_assert(STAGE_BOX * STAGE_BOXES == T && STAGE_BOX % BOX == 0, "stage splits into equal boxes");
     static constexpr int RED_FLOATS = NC * (D + 4);
     static constexpr int OFF_RED = STAGES * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_RED + 2 * RED_FLOATS * 4;
     static constexpr int BAR_COUNT = 2 * STAGES + 2;
     static constexpr int SMEM_BYTES = OFF_BAR + BAR_COUNT * 8 + 16 + 1024;  // + abort flag + base alignment
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget of one CTA");
+    // Tensor-copy destinations in shared memory must be 128-byte aligned, and
+    // the swizzled code tiles 1024-byte aligned (stage bases are 1024-aligned).
+    static_assert((SC_BOX * 4) % 128 == 0 && OFF_KS % 128 == 0 && OFF_VS % 128 == 0, "scale boxes 128B-aligned");
+    static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && (BOX * D) % 1024 == 0 && (STAGE_BOX * D) % 1024 == 0,
+                  "code boxes 1024B-aligned");
+    static_assert(STAGE_BYTES % 1024 == 0 && OFF_Q % 16 == 0 && OFF_META % 16 == 0, "stage layout alignment");
     static constexpr int NI = D / 16;  // q.k MMAs per 16-token block (k = 16 channels each)
     static constexpr int NJ = D / 16;  // p.V MMAs per 16-token block (m = 16 channels each)
 };
@@ -353,17 +372,25 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 meta->vs_off = args.vs_mis + tok - vsx;
                 const uint32_t bytes = nbox * C::BOX * D * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                if (n == (uint32_t)C::T) {  // full stage: one box of T tokens each for K and V
-                    tma_load_2d(st + C::OFF_K, &map_k_stage, &full[slot], 0, (int32_t)tok);
-                    tma_load_2d(st + C::OFF_V, &map_v_stage, &full[slot], 0, (int32_t)tok);
+                if (n == (uint32_t)C::T) {  // full stage: whole-stage boxes for K and V
+#pragma unroll
+                    for (int b = 0; b < C::STAGE_BOXES; ++b) {
+                        tma_load_2d(st + C::OFF_K + b * C::STAGE_BOX * D, &map_k_stage, &full[slot], 0,
+                                    (int32_t)(tok + b * C::STAGE_BOX));
+                        tma_load_2d(st + C::OFF_V + b * C::STAGE_BOX * D, &map_v_stage, &full[slot], 0,
+                                    (int32_t)(tok + b * C::STAGE_BOX));
+                    }
                 } else {  // segment tail: 16-token boxes, none wholly past the segment
                     for (uint32_t b = 0; b < nbox; ++b) {
                         tma_load_2d(st + C::OFF_K + b * C::BOX * D, &map_k, &full[slot], 0, (int32_t)(tok + b * C::BOX));
                         tma_load_2d(st + C::OFF_V + b * C::BOX * D, &map_v, &full[slot], 0, (int32_t)(tok + b * C::BOX));
                     }
                 }
-                tma_load_1d(st + C::OFF_KS, &map_ks, &full[slot], (int32_t)ksx);
-                tma_load_1d(st + C::OFF_VS, &map_vs, &full[slot], (int32_t)vsx);
+#pragma unroll
+                for (int b = 0; b < C::SC_BOXES; ++b) {
+                    tma_load_1d(st + C::OFF_KS + b * C::SC_BOX * 4, &map_ks, &full[slot], (int32_t)(ksx + b * C::SC_BOX));
+                    tma_load_1d(st + C::OFF_VS + b * C::SC_BOX * 4, &map_vs, &full[slot], (int32_t)(vsx + b * C::SC_BOX));
+                }
                 if (first) {
                     const unsigned char* qrow = reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * q_bytes;
                     bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
@@ -436,77 +463,94 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             for (int j = 0; j < C::NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
         }
 
-        const int tok0 = warp * C::BOX;
-        const int nv = (int)nvalid - tok0;
-        // One 16-token block of this warp.  MASKED handles a segment's ragged
-        // last block (tokens >= nv contribute nothing); full blocks skip masking.
-        auto block = [&](auto masked_tag) {
+        const int tok0 = warp * C::TPW;
+        const int nv = (int)nvalid - tok0;  // valid tokens from this warp's first token on
+        // NBLK consecutive 16-token blocks of this warp, interleaved for ILP.
+        // MASKED handles a segment's ragged end (tokens >= nv contribute nothing).
+        auto blocks = [&](auto nblk_tag, auto masked_tag) {
+            constexpr int NBLK = decltype(nblk_tag)::value;
             constexpr bool MASKED = decltype(masked_tag)::value;
             const uint32_t kt = smem_addr(st + C::OFF_K + tok0 * D);
             const uint32_t vt = smem_addr(st + C::OFF_V + tok0 * D);
             const uint32_t ks = smem_addr(st + C::OFF_KS) + (ks_off + tok0) * 4u;
             const uint32_t vs = smem_addr(st + C::OFF_VS) + (vs_off + tok0) * 4u;
-            auto scale = [&](uint32_t addr, int e) -> float {
+            auto scale = [&](uint32_t addr, int e) -> float {  // e: token index from tok0
                 if constexpr (MASKED) return e < nv ? lds_f32(addr + e * 4) : 0.f;
                 else return lds_f32(addr + e * 4);
             };
 
-            // ---- scores: q . k for tokens g and g+8 of this warp's box
-            const float sg = scale(ks, g), sg8 = scale(ks, g + 8);
-            const uint64_t sg2 = f2_pack(sg, sg), sg82 = f2_pack(sg8, sg8);
-            float sacc[4] = {0.f, 0.f, 0.f, 0.f}, sacc2[4] = {0.f, 0.f, 0.f, 0.f};
-            // k_t = bf16(i8 * ks[t]) for 4 channels of token g (a) and g+8 (b),
-            // accumulated against the q fragments of MMA i
-            auto qk_mma = [&](int i, uint32_t wa, uint32_t wb) {
-                uint64_t a01, a23, b01, b23;
-                i8x4_to_f32x2(wa, a01, a23);
-                i8x4_to_f32x2(wb, b01, b23);
-                a01 = f2_mul(a01, sg2);
-                a23 = f2_mul(a23, sg2);
-                b01 = f2_mul(b01, sg82);
-                b23 = f2_mul(b23, sg82);
-                // two independent accumulator chains halve the MMA dependency depth
-                mma_bf16_16816((i & 1) ? sacc2 : sacc, pack_bf16x2_f2(a01), pack_bf16x2_f2(b01),
-                               pack_bf16x2_f2(a23), pack_bf16x2_f2(b23), qb[i][0], qb[i][1]);
-            };
-            if constexpr (D == 128) {
-                // 128B swizzle: row e, 16B chunk x stored at chunk x ^ (e & 7).
-                const uint4 ka0 = lds128(kt + g * 128 + (((2 * c) ^ g) << 4));
-                const uint4 ka1 = lds128(kt + g * 128 + (((2 * c + 1) ^ g) << 4));
-                const uint4 kb0 = lds128(kt + (g + 8) * 128 + (((2 * c) ^ g) << 4));
-                const uint4 kb1 = lds128(kt + (g + 8) * 128 + (((2 * c + 1) ^ g) << 4));
-                qk_mma(0, ka0.x, kb0.x);
-                qk_mma(1, ka0.y, kb0.y);
-                qk_mma(2, ka0.z, kb0.z);
-                qk_mma(3, ka0.w, kb0.w);
-                qk_mma(4, ka1.x, kb1.x);
-                qk_mma(5, ka1.y, kb1.y);
-                qk_mma(6, ka1.z, kb1.z);
-                qk_mma(7, ka1.w, kb1.w);
-            } else {
-                // 64B swizzle: row e, 16B chunk x stored at chunk x ^ ((e >> 1) & 3).
-                const int sw = (g >> 1) & 3;
-                const uint4 ka = lds128(kt + g * 64 + ((c ^ sw) << 4));
-                const uint4 kb = lds128(kt + (g + 8) * 64 + ((c ^ sw) << 4));
-                qk_mma(0, ka.x, kb.x);
-                qk_mma(1, ka.y, kb.y);
-                qk_mma(2, ka.z, kb.z);
-                qk_mma(3, ka.w, kb.w);
-            }
-            float s_g = (sacc[0] + sacc2[0]) + (sacc[1] + sacc2[1]);
-            float s_g8 = (sacc[2] + sacc2[2]) + (sacc[3] + sacc2[3]);
-            s_g += __shfl_xor_sync(0xffffffffu, s_g, 1);
-            s_g8 += __shfl_xor_sync(0xffffffffu, s_g8, 1);
-            s_g += __shfl_xor_sync(0xffffffffu, s_g, 2);
-            s_g8 += __shfl_xor_sync(0xffffffffu, s_g8, 2);
-            if constexpr (MASKED) {
-                if (g >= nv) s_g = -INFINITY;
-                if (g + 8 >= nv) s_g8 = -INFINITY;
+            // ---- scores: q . k for tokens g and g+8 of each block
+            float s_g[NBLK], s_g8[NBLK];
+            {
+                uint64_t sg2[NBLK], sg82[NBLK];
+                float sacc[NBLK][2][4];
+                uint32_t wa[NBLK][C::NI], wb[NBLK][C::NI];
+#pragma unroll
+                for (int b = 0; b < NBLK; ++b) {
+                    const float sg = scale(ks, 16 * b + g), sg8 = scale(ks, 16 * b + g + 8);
+                    sg2[b] = f2_pack(sg, sg);
+                    sg82[b] = f2_pack(sg8, sg8);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) sacc[b][h][0] = sacc[b][h][1] = sacc[b][h][2] = sacc[b][h][3] = 0.f;
+                    const uint32_t kb = kt + b * 16 * D;
+                    if constexpr (D == 128) {
+                        // 128B swizzle: row e, 16B chunk x stored at chunk x ^ (e & 7).
+                        const uint4 ka0 = lds128(kb + g * 128 + (((2 * c) ^ g) << 4));
+                        const uint4 ka1 = lds128(kb + g * 128 + (((2 * c + 1) ^ g) << 4));
+                        const uint4 kb0 = lds128(kb + (g + 8) * 128 + (((2 * c) ^ g) << 4));
+                        const uint4 kb1 = lds128(kb + (g + 8) * 128 + (((2 * c + 1) ^ g) << 4));
+                        wa[b][0] = ka0.x; wa[b][1] = ka0.y; wa[b][2] = ka0.z; wa[b][3] = ka0.w;
+                        wa[b][4] = ka1.x; wa[b][5] = ka1.y; wa[b][6] = ka1.z; wa[b][7] = ka1.w;
+                        wb[b][0] = kb0.x; wb[b][1] = kb0.y; wb[b][2] = kb0.z; wb[b][3] = kb0.w;
+                        wb[b][4] = kb1.x; wb[b][5] = kb1.y; wb[b][6] = kb1.z; wb[b][7] = kb1.w;
+                    } else {
+                        // 64B swizzle: row e, 16B chunk x stored at chunk x ^ ((e >> 1) & 3).
+                        const int sw = (g >> 1) & 3;
+                        const uint4 ka = lds128(kb + g * 64 + ((c ^ sw) << 4));
+                        const uint4 kc = lds128(kb + (g + 8) * 64 + ((c ^ sw) << 4));
+                        wa[b][0] = ka.x; wa[b][1] = ka.y; wa[b][2] = ka.z; wa[b][3] = ka.w;
+                        wb[b][0] = kc.x; wb[b][1] = kc.y; wb[b][2] = kc.z; wb[b][3] = kc.w;
+                    }
+                }
+                // k_t = bf16(i8 * ks[t]) for 4 channels of token g (wa) and g+8 (wb),
+                // against the q fragments of MMA i; two accumulator chains per block
+#pragma unroll
+                for (int i = 0; i < C::NI; ++i) {
+#pragma unroll
+                    for (int b = 0; b < NBLK; ++b) {
+                        uint64_t a01, a23, b01, b23;
+                        i8x4_to_f32x2(wa[b][i], a01, a23);
+                        i8x4_to_f32x2(wb[b][i], b01, b23);
+                        a01 = f2_mul(a01, sg2[b]);
+                        a23 = f2_mul(a23, sg2[b]);
+                        b01 = f2_mul(b01, sg82[b]);
+                        b23 = f2_mul(b23, sg82[b]);
+                        mma_bf16_16816(sacc[b][i & 1], pack_bf16x2_f2(a01), pack_bf16x2_f2(b01),
+                                       pack_bf16x2_f2(a23), pack_bf16x2_f2(b23), qb[i][0], qb[i][1]);
+                    }
+                }
+#pragma unroll
+                for (int b = 0; b < NBLK; ++b) {
+                    float x = (sacc[b][0][0] + sacc[b][1][0]) + (sacc[b][0][1] + sacc[b][1][1]);
+                    float y = (sacc[b][0][2] + sacc[b][1][2]) + (sacc[b][0][3] + sacc[b][1][3]);
+                    x += __shfl_xor_sync(0xffffffffu, x, 1);
+                    y += __shfl_xor_sync(0xffffffffu, y, 1);
+                    x += __shfl_xor_sync(0xffffffffu, x, 2);
+                    y += __shfl_xor_sync(0xffffffffu, y, 2);
+                    if constexpr (MASKED) {
+                        if (16 * b + g >= nv) x = -INFINITY;
+                        if (16 * b + g + 8 >= nv) y = -INFINITY;
+                    }
+                    s_g[b] = x;
+                    s_g8[b] = y;
+                }
             }
 
             // ---- online softmax (base 2) with a lazy reference point: m2 moves
             // only when a score exceeds it by more than kSlack, so p <= 2^kSlack.
-            const float sm = fmaxf(s_g, s_g8);
+            float sm = fmaxf(s_g[0], s_g8[0]);
+#pragma unroll
+            for (int b = 1; b < NBLK; ++b) sm = fmaxf(sm, fmaxf(s_g[b], s_g8[b]));
             if (__any_sync(0xffffffffu, sm > m2 + kSlack)) {
                 float bm = fmaxf(sm, __shfl_xor_sync(0xffffffffu, sm, 4));
                 bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
@@ -522,80 +566,89 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 }
                 m2 = bm;
             }
-            const float p_g = fast_exp2(s_g - m2), p_g8 = fast_exp2(s_g8 - m2);
-            zsum += p_g + p_g8;
 
-            // ---- p as the B operand (k = tokens 2c, 2c+1, 2c+8, 2c+9; n = term g).
-            // Lane (G, c) holds term c of its tokens G and G+8; thread (g, c) pulls
-            // term g of tokens 2c, 2c+1 from the lanes of groups 2c, 2c+1.
-            uint32_t terms;
-            {
-                const uint32_t h = pack_bf16x2(p_g, p_g8);
-                const float r0 = p_g - bf16_lo_to_f32(h), r1 = p_g8 - bf16_hi_to_f32(h);
-                const uint32_t l = pack_bf16x2(r0, r1);
-                const uint32_t l2 = pack_bf16x2(r0 - bf16_lo_to_f32(l), r1 - bf16_hi_to_f32(l));
-                terms = c == 0 ? h : c == 1 ? l : c == 2 ? l2 : 0u;
-            }
-            const uint32_t tx = __shfl_sync(0xffffffffu, terms, 8 * c + (g & 3));
-            const uint32_t ty = __shfl_sync(0xffffffffu, terms, 8 * c + 4 + (g & 3));
-            const uint32_t pb0 = g < 3 ? __byte_perm(tx, ty, 0x5410) : 0u;
-            const uint32_t pb1 = g < 3 ? __byte_perm(tx, ty, 0x7632) : 0u;
+#pragma unroll
+            for (int b = 0; b < NBLK; ++b) {
+                const float p_g = fast_exp2(s_g[b] - m2), p_g8 = fast_exp2(s_g8[b] - m2);
+                zsum += p_g + p_g8;
+                // p as the B operand (k = tokens 2c, 2c+1, 2c+8, 2c+9; n = term g).
+                // Lane (G, c) holds term c of its tokens G and G+8; thread (g, c)
+                // pulls term g of tokens 2c, 2c+1 from the lanes of groups 2c, 2c+1.
+                uint32_t terms;
+                {
+                    const uint32_t h = pack_bf16x2(p_g, p_g8);
+                    const float r0 = p_g - bf16_lo_to_f32(h), r1 = p_g8 - bf16_hi_to_f32(h);
+                    const uint32_t l = pack_bf16x2(r0, r1);
+                    const uint32_t l2 = pack_bf16x2(r0 - bf16_lo_to_f32(l), r1 - bf16_hi_to_f32(l));
+                    terms = c == 0 ? h : c == 1 ? l : c == 2 ? l2 : 0u;
+                }
+                const uint32_t tx = __shfl_sync(0xffffffffu, terms, 8 * c + (g & 3));
+                const uint32_t ty = __shfl_sync(0xffffffffu, terms, 8 * c + 4 + (g & 3));
+                const uint32_t pb0 = g < 3 ? __byte_perm(tx, ty, 0x5410) : 0u;
+                const uint32_t pb1 = g < 3 ? __byte_perm(tx, ty, 0x7632) : 0u;
 
-            // ---- p . V: A = V^T (rows = channels, k = tokens 2c, 2c+1, 2c+8, 2c+9)
-            const int e0 = 2 * c, e1 = 2 * c + 1, e2 = 2 * c + 8, e3 = 2 * c + 9;
-            const float v0s = scale(vs, e0), v1s = scale(vs, e1), v2s = scale(vs, e2), v3s = scale(vs, e3);
-            const uint64_t s0 = f2_pack(v0s, v0s), s1 = f2_pack(v1s, v1s);
-            const uint64_t s2 = f2_pack(v2s, v2s), s3 = f2_pack(v3s, v3s);
-            // channels x..x+3 of the four tokens (words w0..w3) -> 4 MMAs, starting
-            // at accumulator j0 (channel rows of the A tile: m = g -> word wa, m = g+8 -> word wb)
-            auto pv_mma4 = [&](int j0, uint32_t wa0, uint32_t wa1, uint32_t wa2, uint32_t wa3, uint32_t wb0,
-                               uint32_t wb1, uint32_t wb2, uint32_t wb3) {
-                uint64_t a[4][2], b[4][2];  // [token][pair]: channels (x, x+1), (x+2, x+3)
-                i8x4_to_f32x2(wa0, a[0][0], a[0][1]);
-                i8x4_to_f32x2(wa1, a[1][0], a[1][1]);
-                i8x4_to_f32x2(wa2, a[2][0], a[2][1]);
-                i8x4_to_f32x2(wa3, a[3][0], a[3][1]);
-                i8x4_to_f32x2(wb0, b[0][0], b[0][1]);
-                i8x4_to_f32x2(wb1, b[1][0], b[1][1]);
-                i8x4_to_f32x2(wb2, b[2][0], b[2][1]);
-                i8x4_to_f32x2(wb3, b[3][0], b[3][1]);
-                const uint64_t sc[4] = {s0, s1, s2, s3};
-                float fa[4][4], fb[4][4];
+                // ---- p . V: A = V^T (rows = channels, k = tokens 2c, 2c+1, 2c+8, 2c+9)
+                const int e0 = 16 * b + 2 * c, e1 = e0 + 1, e2 = e0 + 8, e3 = e0 + 9;
+                const float v0s = scale(vs, e0), v1s = scale(vs, e1), v2s = scale(vs, e2), v3s = scale(vs, e3);
+                const uint64_t s0 = f2_pack(v0s, v0s), s1 = f2_pack(v1s, v1s);
+                const uint64_t s2 = f2_pack(v2s, v2s), s3 = f2_pack(v3s, v3s);
+                // channels x..x+3 of the four tokens (words w0..w3) -> 4 MMAs, starting at
+                // accumulator j0 (channel rows of the A tile: m = g -> word wa, m = g+8 -> word wb)
+                auto pv_mma4 = [&](int j0, uint32_t wa0, uint32_t wa1, uint32_t wa2, uint32_t wa3, uint32_t wb0,
+                                   uint32_t wb1, uint32_t wb2, uint32_t wb3) {
+                    uint64_t a[4][2], bb[4][2];  // [token][pair]: channels (x, x+1), (x+2, x+3)
+                    i8x4_to_f32x2(wa0, a[0][0], a[0][1]);
+                    i8x4_to_f32x2(wa1, a[1][0], a[1][1]);
+                    i8x4_to_f32x2(wa2, a[2][0], a[2][1]);
+                    i8x4_to_f32x2(wa3, a[3][0], a[3][1]);
+                    i8x4_to_f32x2(wb0, bb[0][0], bb[0][1]);
+                    i8x4_to_f32x2(wb1, bb[1][0], bb[1][1]);
+                    i8x4_to_f32x2(wb2, bb[2][0], bb[2][1]);
+                    i8x4_to_f32x2(wb3, bb[3][0], bb[3][1]);
+                    const uint64_t sc[4] = {s0, s1, s2, s3};
+                    float fa[4][4], fb[4][4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    f2_unpack(f2_mul(a[t][0], sc[t]), fa[t][0], fa[t][1]);
-                    f2_unpack(f2_mul(a[t][1], sc[t]), fa[t][2], fa[t][3]);
-                    f2_unpack(f2_mul(b[t][0], sc[t]), fb[t][0], fb[t][1]);
-                    f2_unpack(f2_mul(b[t][1], sc[t]), fb[t][2], fb[t][3]);
-                }
+                    for (int t = 0; t < 4; ++t) {
+                        f2_unpack(f2_mul(a[t][0], sc[t]), fa[t][0], fa[t][1]);
+                        f2_unpack(f2_mul(a[t][1], sc[t]), fa[t][2], fa[t][3]);
+                        f2_unpack(f2_mul(bb[t][0], sc[t]), fb[t][0], fb[t][1]);
+                        f2_unpack(f2_mul(bb[t][1], sc[t]), fb[t][2], fb[t][3]);
+                    }
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    mma_bf16_16816(acc[j0 + e], pack_bf16x2(fa[0][e], fa[1][e]), pack_bf16x2(fb[0][e], fb[1][e]),
-                                   pack_bf16x2(fa[2][e], fa[3][e]), pack_bf16x2(fb[2][e], fb[3][e]), pb0, pb1);
+                    for (int e = 0; e < 4; ++e) {
+                        mma_bf16_16816(acc[j0 + e], pack_bf16x2(fa[0][e], fa[1][e]), pack_bf16x2(fb[0][e], fb[1][e]),
+                                       pack_bf16x2(fa[2][e], fa[3][e]), pack_bf16x2(fb[2][e], fb[3][e]), pb0, pb1);
+                    }
+                };
+                if constexpr (D == 128) {
+                    // thread holds channels [16g, 16g+16) of its four tokens; rows e0..e3
+                    // of this block sit at 128B swizzle phase (e & 7) == (2c, 2c+1, 2c, 2c+1)
+                    const uint32_t vb = vt + b * 16 * 128;
+                    const uint4 v0 = lds128(vb + (2 * c) * 128 + ((g ^ (2 * c)) << 4));
+                    const uint4 v1 = lds128(vb + (2 * c + 1) * 128 + ((g ^ (2 * c + 1)) << 4));
+                    const uint4 v2 = lds128(vb + (2 * c + 8) * 128 + ((g ^ (2 * c)) << 4));
+                    const uint4 v3 = lds128(vb + (2 * c + 9) * 128 + ((g ^ (2 * c + 1)) << 4));
+                    // accumulator j: channel 16g + j (m = g) and 16g + 8 + j (m = g + 8)
+                    pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.z, v1.z, v2.z, v3.z);
+                    pv_mma4(4, v0.y, v1.y, v2.y, v3.y, v0.w, v1.w, v2.w, v3.w);
+                } else {
+                    // thread holds channels [8g, 8g+8) of its four tokens
+                    const uint32_t vb = vt + b * 16 * 64;
+                    const uint32_t off = ((((uint32_t)g >> 1) ^ (uint32_t)c) << 4) + (((uint32_t)g & 1u) << 3);
+                    const uint2 v0 = lds64(vb + (2 * c) * 64 + off);
+                    const uint2 v1 = lds64(vb + (2 * c + 1) * 64 + off);
+                    const uint2 v2 = lds64(vb + (2 * c + 8) * 64 + off);
+                    const uint2 v3 = lds64(vb + (2 * c + 9) * 64 + off);
+                    // accumulator j: channel 8g + j (m = g) and 8g + 4 + j (m = g + 8)
+                    pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.y, v1.y, v2.y, v3.y);
                 }
-            };
-            if constexpr (D == 128) {
-                // thread holds channels [16g, 16g+16) of its four tokens
-                const uint4 v0 = lds128(vt + e0 * 128 + ((g ^ e0) << 4));
-                const uint4 v1 = lds128(vt + e1 * 128 + ((g ^ e1) << 4));
-                const uint4 v2 = lds128(vt + e2 * 128 + ((g ^ (e2 & 7)) << 4));
-                const uint4 v3 = lds128(vt + e3 * 128 + ((g ^ (e3 & 7)) << 4));
-                // accumulator j: channel 16g + j (m = g) and 16g + 8 + j (m = g + 8)
-                pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.z, v1.z, v2.z, v3.z);
-                pv_mma4(4, v0.y, v1.y, v2.y, v3.y, v0.w, v1.w, v2.w, v3.w);
-            } else {
-                // thread holds channels [8g, 8g+8) of its four tokens
-                const uint32_t off = ((((uint32_t)g >> 1) ^ (uint32_t)c) << 4) + (((uint32_t)g & 1u) << 3);
-                const uint2 v0 = lds64(vt + e0 * 64 + off);
-                const uint2 v1 = lds64(vt + e1 * 64 + off);
-                const uint2 v2 = lds64(vt + e2 * 64 + off);
-                const uint2 v3 = lds64(vt + e3 * 64 + off);
-                // accumulator j: channel 8g + j (m = g) and 8g + 4 + j (m = g + 8)
-                pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.y, v1.y, v2.y, v3.y);
             }
         };
-        if (nv >= C::BOX) block(std::false_type{});
-        else if (nv > 0) block(std::true_type{});
+        using I1 = std::integral_constant<int, 1>;
+        using INB = std::integral_constant<int, C::NB>;
+        if (nv >= C::TPW) blocks(INB{}, std::false_type{});
+        else if (nv > C::BOX && C::NB > 1) blocks(INB{}, std::true_type{});
+        else if (nv > 0) blocks(I1{}, std::true_type{});
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
 
@@ -613,13 +666,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 a += __shfl_xor_sync(0xffffffffu, a, 2);
                 b += __shfl_xor_sync(0xffffffffu, b, 2);
                 if (c == (j & 3)) {
-                    if constexpr (D == 128) {
-                        mine[16 * g + j] = a;
-                        mine[16 * g + 8 + j] = b;
-                    } else {
-                        mine[8 * g + j] = a;
-                        mine[8 * g + 4 + j] = b;
-                    }
+                    // accumulator j holds channels (D/8) g + j and (D/8) g + D/16 + j
+                    mine[(D / 8) * g + j] = a;
+                    mine[(D / 8) * g + D / 16 + j] = b;
                 }
             }
             float zt = zsum;
@@ -818,7 +867,7 @@ cudaError_t configure_attention_kernels(int /*device*/) {
 }
 
 uint32_t attention_scale_box_elems() { return Cfg<128>::SC_BOX; }
-uint32_t attention_stage_tokens() { return Cfg<128>::T; }
+uint32_t attention_stage_tokens() { return Cfg<128>::STAGE_BOX; }
 
 cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
     PlanArgs a{};
