@@ -158,6 +158,26 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
                                  const uint32_t* lengths, void* out, void* workspace,
                                  size_t workspace_bytes, uint32_t* status, void* stream);
 
+/* pp_b200_decode_attention for callers that cannot allocate device memory
+ * when they call attention (a host that passes a plugin only its input and
+ * output buffers, a serving loop that forbids cudaMalloc after start-up).
+ * No counterpart in the reference: its CustomOp allocates per call.
+ * Same arguments and results as pp_b200_decode_attention, without the
+ * workspace: the plan and split-K partials live in a 4 MiB scratch array
+ * compiled into the library, which every GPU that loads the library keeps
+ * until the process exits.  Geometries whose workspace
+ * (pp_b200_attention_workspace_size) exceeds 4 MiB are rejected with
+ * PP_STATUS_PRECONDITION; PP_ATTN_PLAN_READY is rejected (the scratch is
+ * re-planned on every call).  Nothing in the scratch needs to start at zero.
+ * All calls share the one array: calls that may run at the same time on the
+ * GPU (different streams, or several host threads) race and must be
+ * serialised by the caller.  The first call on each device looks up the
+ * array's device address; make that first call before any stream capture.
+ * Nothing is allocated: no cudaMalloc, cudaFree or allocating library call. */
+int32_t pp_b200_decode_attention_static(const PpKvArena* arena, const PpAttnParams* params, const void* q,
+                                        const float* scratch_k, const float* scratch_v,
+                                        const uint32_t* lengths, void* out, uint32_t* status, void* stream);
+
 /* Decodes device status bits into a message (static storage). */
 const char* pp_b200_status_message(uint32_t status_bits);
 

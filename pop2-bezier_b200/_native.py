@@ -38,6 +38,7 @@ EXPORTED = (
     "pp_b200_attention_workspace_size",
     "pp_b200_plan_ragged",
     "pp_b200_decode_attention",
+    "pp_b200_decode_attention_static",
     "pp_b200_status_message",
     "pp_b200_checked_batch_rows",
     "pp_b200_check_write_offsets",
@@ -104,6 +105,7 @@ def _load() -> C.CDLL:
         "pp_b200_attention_workspace_size": (sz, [P(PpKvArena), P(PpAttnParams)]),
         "pp_b200_plan_ragged": (i32, [P(PpKvArena), P(PpAttnParams), vp, u32, vp, sz, vp]),
         "pp_b200_decode_attention": (i32, [P(PpKvArena), P(PpAttnParams), vp, vp, vp, vp, vp, vp, sz, vp, vp]),
+        "pp_b200_decode_attention_static": (i32, [P(PpKvArena), P(PpAttnParams), vp, vp, vp, vp, vp, vp, vp]),
         "pp_b200_status_message": (C.c_char_p, [u32]),
         "pp_b200_checked_batch_rows": (i32, [u64, u32, P(u64)]),
         "pp_b200_check_write_offsets": (i32, [P(u64), u64, u32, u32, u32]),

@@ -27,6 +27,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
 SOURCES = [
     ("csrc/kernels/quant.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
     ("csrc/kernels/attention.cu", []),
+    ("csrc/kernels/attention_static.cu", []),
     ("csrc/host/abi.cpp", []),
     ("csrc/host/sched.cpp", []),
     ("csrc/host/selfcheck.cpp", []),
