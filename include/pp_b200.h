@@ -10,7 +10,10 @@
  *   - every entry point returns an int32 status:
  *       PP_STATUS_OK (0)             success
  *       PP_STATUS_PRECONDITION (1)   invalid geometry/argument: nothing was launched
- *       PP_STATUS_INVALID_OUTPUT (2) a device check found invalid data (see pp_b200_read_status)
+ *       PP_STATUS_INVALID_OUTPUT (2) the class a caller reports when the device status word
+ *                                    (PP_DEV_* bits below, text from pp_b200_status_message)
+ *                                    is non-zero after the stream completes; kernels cannot
+ *                                    return it, so no entry point does
  *       PP_STATUS_UNCERTAIN (3)      a CUDA launch/runtime error: device state uncertain,
  *                                    the caller must discard the KV state (reload)
  *   - pp_b200_last_error() returns a thread-local UTF-8 message for the last

@@ -149,3 +149,42 @@ def partition_branches(costs: list[int], shards: int) -> tuple[list[int], list[i
     cost = (C.c_uint64 * max(1, shards))()
     N.check(N.lib.pp_b200_sched_partition(arr, n, shards, out, cost))
     return [int(out[i]) for i in range(n)], [int(cost[s]) for s in range(shards)]
+
+
+class BranchShards:
+    """The branches one rank owns, and the gather of their outputs to rank 0.
+
+    Branches are independent (app/src/inference/batch.rs:241-558 runs each
+    branch's decode on its own cache), so a step needs no collective: each rank
+    decodes its shard of the LPT partition above, and only the final outputs
+    travel, once, to rank 0.  Shards may hold different numbers of branches;
+    the gather pads every shard to the largest and rank 0 puts the rows back
+    in global branch order.
+    """
+
+    def __init__(self, costs: list[int], world: int, rank: int):
+        if not 0 <= rank < world:
+            raise N.PreconditionError(f"rank {rank} outside world of {world}")
+        self.world, self.rank = world, rank
+        self.shard_of, self.shard_cost = partition_branches(costs, world)
+        self.members = [[b for b, s in enumerate(self.shard_of) if s == r] for r in range(world)]
+        self.mine = self.members[rank]
+        self.widest = max(len(m) for m in self.members)
+
+    def gather(self, dist, out: torch.Tensor) -> torch.Tensor | None:
+        """`out` is this rank's output, leading dim = len(self.mine) branches.
+        Every rank must call this (it is one collective); rank 0 gets the
+        outputs of all branches in global order, the other ranks get None."""
+        if out.shape[0] != len(self.mine):
+            raise N.PreconditionError(f"gather: {out.shape[0]} branch outputs for a shard of {len(self.mine)}")
+        padded = out.new_zeros((self.widest, *out.shape[1:]))
+        padded[: len(self.mine)] = out
+        parts = [torch.empty_like(padded) for _ in range(self.world)] if self.rank == 0 else None
+        dist.gather(padded, parts, dst=0)
+        if self.rank != 0:
+            return None
+        full = out.new_empty((len(self.shard_of), *out.shape[1:]))
+        for r, branches in enumerate(self.members):
+            if branches:
+                full[torch.tensor(branches, device=out.device)] = parts[r][: len(branches)]
+        return full
