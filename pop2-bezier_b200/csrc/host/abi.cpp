@@ -327,7 +327,8 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     cudaError_t e;
     if (!L.plan_ready && (e = pp::launch_plan(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 plan launch");
     if ((e = pp::launch_attention(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 attention launch");
-    if ((e = pp::launch_combine(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 combine launch");
+    // stream-K plans are finished inside the attention kernel; fixed splits need the combine
+    if (L.split && (e = pp::launch_combine(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 combine launch");
     return PP_STATUS_OK;
 }
 

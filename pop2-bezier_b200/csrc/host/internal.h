@@ -19,8 +19,15 @@ namespace pp {
 //   cta_seg   u32 [max_ctas + 1]  first segment of each CTA
 //   segs      SegDesc [max_segs]
 //   partials  f32 [max_segs][head_dim + 4]   acc[0..D), m (log2 units), z
+//   row_cnt   u32 [rows]      finished segments per row (zero between calls)
+//   orphans   u32 [rows]      rows without segments (invalid, or reference
+//                             mode with no history: only the scratch token)
 // A segment is a contiguous token range of one row processed by one CTA and
-// producing one partial (m, z, acc) for the log-sum-exp combine.
+// producing one partial (m, z, acc) for the log-sum-exp combine.  With
+// stream-K segments the attention kernel also finishes the rows: a row held
+// by one segment is normalised in place, and of a row split over several
+// CTAs the CTA that completes it last (row_cnt) merges the partials.  Fixed
+// splits leave the merge to the combine kernel.
 
 constexpr uint32_t kInvalidRow = 0xffffffffu;
 
@@ -36,15 +43,16 @@ struct PlanHeader {
     uint32_t scratch;
     uint32_t max_segs;
     uint32_t max_ctas;
-    uint32_t pad[3];
+    uint32_t n_orphans;
+    uint32_t pad[2];
 };
 
 struct SegDesc {
-    uint32_t row, t0, t1, pad;
+    uint32_t row, t0, t1, row_segs;  // row_segs: segments of this row
 };
 
 struct WsLayout {
-    size_t row_len, row_seg, cta_seg, segs, partials, total;
+    size_t row_len, row_seg, cta_seg, segs, partials, row_cnt, orphans, total;
     uint32_t max_segs, max_ctas;
 };
 
@@ -69,6 +77,10 @@ inline WsLayout ws_layout(uint32_t rows, uint32_t capacity, uint32_t head_dim, u
     off = align_up(off + sizeof(SegDesc) * (size_t)l.max_segs, 256);
     l.partials = off;
     off = align_up(off + 4ull * (head_dim + 4) * (size_t)l.max_segs, 256);
+    l.row_cnt = off;
+    off = align_up(off + 4ull * rows, 256);
+    l.orphans = off;
+    off = align_up(off + 4ull * rows, 256);
     l.total = off;
     return l;
 }

@@ -19,8 +19,11 @@
 //     a packed f32 add removes the bias exactly, a packed f32 multiply
 //     applies the scale (the reference's f32 product) and a bf16x2 pack
 //     rounds to nearest even, so bf16(i8 * scale) is reproduced bit for bit.
-//   * combine_kernel merges the per-segment partials (and, in reference mode,
-//     the scratch token) with a log-sum-exp combine.
+//   * rows end with a log-sum-exp merge of their per-segment partials (and,
+//     in reference mode, the scratch token).  With stream-K plans the
+//     attention kernel does it: a row held by one segment is normalised in
+//     place, a row split over CTAs by the CTA that completes it last.  With
+//     fixed splits, combine_kernel does it after the attention kernel.
 // All softmax arithmetic runs in base 2 (scores pre-scaled by log2 e).
 #include <type_traits>
 
@@ -77,6 +80,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     uint32_t* row_seg = reinterpret_cast<uint32_t*>(a.ws + a.l.row_seg);
     uint32_t* cta_seg = reinterpret_cast<uint32_t*>(a.ws + a.l.cta_seg);
     SegDesc* segs = reinterpret_cast<SegDesc*>(a.ws + a.l.segs);
+    uint32_t* row_cnt = reinterpret_cast<uint32_t*>(a.ws + a.l.row_cnt);
+    uint32_t* orphans = reinterpret_cast<uint32_t*>(a.ws + a.l.orphans);
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
 
@@ -121,8 +126,9 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     __syncthreads();
     const uint32_t per = s_per_cta;
 
-    // Pass 2: token prefix -> segment counts -> segment prefix -> descriptors.
-    uint32_t tok_carry = 0, seg_carry = 0;
+    // Pass 2: token prefix -> segment counts -> segment prefix -> descriptors;
+    // rows without segments go to the orphan list.
+    uint32_t tok_carry = 0, seg_carry = 0, orphan_carry = 0;
     for (uint32_t base = 0; base < a.rows; base += blockDim.x) {
         const uint32_t r = base + threadIdx.x;
         bool valid = true;
@@ -137,19 +143,24 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
         }
         const uint32_t s0 = seg_carry + block_exclusive_scan(n, warp_tot, tot);
         seg_carry += tot;
+        const uint32_t orphan = (r < a.rows && n == 0) ? 1u : 0u;
+        const uint32_t o0 = orphan_carry + block_exclusive_scan(orphan, warp_tot, tot);
+        orphan_carry += tot;
         if (r < a.rows) {
             row_seg[r] = s0;
+            row_cnt[r] = 0u;
+            if (orphan) orphans[o0] = r;
             if (a.split) {
                 for (uint32_t k = 0; k < n; ++k) {
                     uint32_t t0 = k * a.split, t1 = min(h, t0 + a.split);
-                    segs[s0 + k] = SegDesc{r, t0, t1, 0u};
+                    segs[s0 + k] = SegDesc{r, t0, t1, n};
                 }
             } else if (n) {
                 const uint32_t j0 = p0 / per;
                 for (uint32_t k = 0; k < n; ++k) {
                     const uint32_t j = j0 + k;
                     const uint32_t lo = max(p0, j * per), hi = min(p0 + h, (j + 1) * per);
-                    segs[s0 + k] = SegDesc{r, lo - p0, hi - p0, 0u};
+                    segs[s0 + k] = SegDesc{r, lo - p0, hi - p0, n};
                     if (j * per >= p0) cta_seg[j] = s0 + k;  // CTA j starts inside this row
                 }
             }
@@ -178,21 +189,123 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
         hdr->scratch = a.scratch;
         hdr->max_segs = a.l.max_segs;
         hdr->max_ctas = a.max_ctas;
+        hdr->n_orphans = orphan_carry;
     }
 }
+
+template <typename T>
+__device__ __forceinline__ float ldq(const T* p, uint64_t i);
+template <>
+__device__ __forceinline__ float ldq<float>(const float* p, uint64_t i) {
+    return p[i];
+}
+template <>
+__device__ __forceinline__ float ldq<__nv_bfloat16>(const __nv_bfloat16* p, uint64_t i) {
+    return __bfloat162float(p[i]);
+}
+
+template <typename O>
+__device__ __forceinline__ void st_out(O* p, uint64_t i, float v);
+template <>
+__device__ __forceinline__ void st_out<float>(float* p, uint64_t i, float v) {
+    p[i] = v;
+}
+template <>
+__device__ __forceinline__ void st_out<__nv_bfloat16>(__nv_bfloat16* p, uint64_t i, float v) {
+    p[i] = __float2bfloat16_rn(v);
+}
+
+
+// Log-sum-exp finish of row r by one warp (lane l owns channels [l*E, l*E+E),
+// E = D/32): merges the row's n partials (m in log2 units, z, acc), fetched in
+// segment order from `part`, and in reference mode the f32 scratch token
+// (q.sk, sv), then writes acc / z.  The merge of pp_i8_merge
+// (int8_kv.cu:53-59) with the scratch token of pp_i8_attention (:36-37, 49)
+// folded in; an invalid row, or one whose weights sum to zero, is NaN.
+template <int D, typename QT, typename OT, typename Part>
+__device__ __forceinline__ void finish_row(int lane, uint32_t r, uint32_t n, bool invalid, const Part& part,
+                                           const void* q, const float* sk, const float* sv, float scale_log2,
+                                           void* out_base) {
+    constexpr int E = D / 32;
+    OT* out = reinterpret_cast<OT*>(out_base) + (uint64_t)r * D;
+    if (invalid) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, __uint_as_float(0x7fc00000u));
+        return;
+    }
+    float mx = -INFINITY;
+    for (uint32_t s = 0; s < n; ++s) mx = fmaxf(mx, part.m(s));
+    float ms = -INFINITY;
+    if (sk) {
+        const QT* qr = reinterpret_cast<const QT*>(q) + (uint64_t)r * D;
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dot += (ldq<QT>(qr, lane * E + e) * scale_log2) * sk[(uint64_t)r * D + lane * E + e];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        ms = dot;
+        mx = fmaxf(mx, ms);
+    }
+    float acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    float z = 0.f;
+    for (uint32_t s = 0; s < n; ++s) {
+        const float m = part.m(s);
+        const float f = m == -INFINITY ? 0.f : fast_exp2(m - mx);
+        z += part.z(s) * f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += part.acc(s, lane, e) * f;
+    }
+    if (sk) {
+        const float f = fast_exp2(ms - mx);
+        z += f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += sv[(uint64_t)r * D + lane * E + e] * f;
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, z > 0.f ? acc[e] / z : __uint_as_float(0x7fc00000u));
+}
+
+// Partials of one row in the workspace, [segment][D + 4] from `base`.
+// Coherent: read through L2 only (partials written by other CTAs of the
+// same launch); otherwise plain loads.
+template <int D, bool Coherent>
+struct GlobalPartials {
+    const float* base;
+    __device__ __forceinline__ float ld(const float* p) const {
+        if constexpr (Coherent) return __ldcg(p);
+        else return *p;
+    }
+    __device__ __forceinline__ float m(uint32_t s) const { return ld(base + (uint64_t)s * (D + 4) + D); }
+    __device__ __forceinline__ float z(uint32_t s) const { return ld(base + (uint64_t)s * (D + 4) + D + 1); }
+    __device__ __forceinline__ float acc(uint32_t s, int lane, int e) const {
+        return ld(base + (uint64_t)s * (D + 4) + lane * (D / 32) + e);
+    }
+};
+
+// The single partial of a row, held in registers (the lane's E channels).
+template <int D>
+struct RegPartial {
+    float mv, zv;
+    float a[D / 32];
+    __device__ __forceinline__ float m(uint32_t) const { return mv; }
+    __device__ __forceinline__ float z(uint32_t) const { return zv; }
+    __device__ __forceinline__ float acc(uint32_t, int, int e) const { return a[e]; }
+};
 
 // ------------------------------------------------------------- attention
 
 // Consumer warps per CTA, 16-token MMA blocks per warp per stage, and ring
 // depth (tuning knobs; the defaults were chosen by measurement on B200).
 #ifndef PP_ATTN_NC
-#define PP_ATTN_NC 11
+#define PP_ATTN_NC 15
 #endif
 #ifndef PP_ATTN_NB
-#define PP_ATTN_NB 2
+#define PP_ATTN_NB 1
 #endif
 #ifndef PP_ATTN_STAGES_D128
-#define PP_ATTN_STAGES_D128 2
+#define PP_ATTN_STAGES_D128 3
 #endif
 #ifndef PP_ATTN_STAGES_D64
 #define PP_ATTN_STAGES_D64 4
@@ -226,7 +339,7 @@ struct Cfg {
     static constexpr int RED_FLOATS = NC * (D + 4);
     static constexpr int OFF_RED = STAGES * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_RED + 2 * RED_FLOATS * 4;
-    static constexpr int BAR_COUNT = 2 * STAGES + 2;
+    static constexpr int BAR_COUNT = 2 * STAGES + 4;  // full, empty, reduction ready x2, reduction free x2
     static constexpr int SMEM_BYTES = OFF_BAR + BAR_COUNT * 8 + 16 + 1024;  // + abort flag + base alignment
     static_assert(SMEM_BYTES <= 232448, "shared memory budget of one CTA");
     // Tensor-copy destinations in shared memory must be 128-byte aligned, and
@@ -240,19 +353,25 @@ struct Cfg {
 };
 
 struct StageMeta {
-    uint32_t row, t, nvalid, slot, flags, ks_off, vs_off, pad;
+    uint32_t row, t, nvalid, slot, flags, ks_off, vs_off, row_segs;
 };
 constexpr uint32_t kFirst = 1u, kLast = 2u, kTerm = 4u;
 
 struct AttnArgs {
     const void* q;
-    const unsigned char* ws;
+    unsigned char* ws;
     float* partials;
     WsLayout l;
     uint32_t capacity;
     uint32_t ks_mis, vs_mis;
     float scale_log2;
     uint32_t* status;
+    // row finish (stream-K plans): outputs, reference-mode scratch token
+    uint32_t finish;    // 1: this kernel writes the outputs; 0: the combine kernel does
+    uint32_t out_bf16;  // output element type: bf16 (1) or f32 (0)
+    void* out;
+    const float* sk;
+    const float* sv;
 };
 
 template <typename QT>
@@ -303,8 +422,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* empty = full + C::STAGES;
-    uint64_t* red_bar = empty + C::STAGES;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 2);
+    uint64_t* red_bar = empty + C::STAGES;  // [2]: all consumer warps' states are in reduction buffer p
+    uint64_t* red_free = red_bar + 2;       // [2]: the finishing warp has read reduction buffer p
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(red_free + 2);
     float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -315,6 +435,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
         mbar_init(&red_bar[0], C::NC);
         mbar_init(&red_bar[1], C::NC);
+        mbar_init(&red_free[0], 1);
+        mbar_init(&red_free[1], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -370,6 +492,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 meta->flags = (first ? kFirst : 0u) | (last ? kLast : 0u);
                 meta->ks_off = args.ks_mis + tok - ksx;
                 meta->vs_off = args.vs_mis + tok - vsx;
+                meta->row_segs = sd.row_segs;
                 const uint32_t bytes = nbox * C::BOX * D * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 if (n == (uint32_t)C::T) {  // full stage: whole-stage boxes for K and V
@@ -426,9 +549,25 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     for (int j = 0; j < C::NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 #pragma unroll
     for (int i = 0; i < C::NI; ++i) qb[i][0] = qb[i][1] = 0u;
-    uint32_t red_phase_bits = 0u;  // bit p: parity to wait for on red_bar[p]
     uint32_t seg_count = 0;
     float* partials = args.partials;
+    uint32_t* row_cnt = reinterpret_cast<uint32_t*>(args.ws + args.l.row_cnt);
+    const uint32_t* row_seg = reinterpret_cast<const uint32_t*>(args.ws + args.l.row_seg);
+    // writes output row r from its n partials (stream-K plans only)
+    auto finish_out = [&](uint32_t r, uint32_t n, const auto& part) {
+        const bool invalid = n == 0 && __ldg(reinterpret_cast<const uint32_t*>(args.ws + args.l.row_len) + r) == kInvalidRow;
+        if (args.out_bf16)
+            finish_row<D, QT, __nv_bfloat16>(lane, r, n, invalid, part, args.q, args.sk, args.sv, args.scale_log2, args.out);
+        else
+            finish_row<D, QT, float>(lane, r, n, invalid, part, args.q, args.sk, args.sv, args.scale_log2, args.out);
+    };
+    if (args.finish) {
+        // rows without segments: invalid (NaN) or, in reference mode, the scratch token alone
+        const uint32_t n_orphans = hdr->n_orphans;
+        const uint32_t* orphans = reinterpret_cast<const uint32_t*>(args.ws + args.l.orphans);
+        for (uint32_t k = blockIdx.x * C::NC + warp; k < n_orphans; k += gridDim.x * C::NC)
+            finish_out(orphans[k], 0u, GlobalPartials<D, false>{partials});
+    }
 
     for (uint32_t it = 0;; ++it) {
         const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
@@ -438,7 +577,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             return;
         }
         unsigned char* st = smem + slot * C::STAGE_BYTES;
-        // StageMeta {row, t, nvalid, slot | flags, ks_off, vs_off, pad}
+        // StageMeta {row, t, nvalid, slot | flags, ks_off, vs_off, row_segs}
         const uint4 m0 = lds128(smem_addr(st + C::OFF_META));
         const uint4 m1 = lds128(smem_addr(st + C::OFF_META) + 16u);
         const uint32_t flags = m1.x;
@@ -653,10 +792,19 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         if (lane == 0) mbar_arrive(&empty[slot]);
 
         if (flags & kLast) {
-            // ---- segment epilogue: merge the NC warp states into one partial
-            const uint32_t par = seg_count & 1u;
+            // ---- segment end: every warp leaves its state (m, z, acc) in reduction
+            // buffer `par`; one warp per segment (in turn) merges the states into the
+            // segment's partial and, with stream-K plans, finishes the row, while the
+            // other warps go on with the next stage.
+            const uint32_t par = seg_count & 1u, use = seg_count >> 1;
             float* buf = red + par * C::RED_FLOATS;
             float* mine = buf + warp * (D + 4);
+            // the previous use of this buffer has been read by its finishing warp
+            if (!mbar_wait_bounded(&red_free[par], (use & 1u) ^ 1u, abort_flag, kWaitLimitNs)) {
+                *abort_flag = 1;
+                if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+                return;
+            }
 #pragma unroll
             for (int j = 0; j < C::NJ; ++j) {
                 float a = acc[j][0] + acc[j][1];
@@ -681,28 +829,59 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_bar[par]);
-            if (!mbar_wait_bounded(&red_bar[par], (red_phase_bits >> par) & 1u, abort_flag, kWaitLimitNs)) {
-                *abort_flag = 1;
-                if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
-                return;
-            }
-            red_phase_bits ^= 1u << par;
-            float* dst = partials + (uint64_t)seg_slot * (D + 4);
-            float mx = -INFINITY;
+            if (warp == (int)(seg_count % C::NC)) {
+                if (!mbar_wait_bounded(&red_bar[par], use & 1u, abort_flag, kWaitLimitNs)) {
+                    *abort_flag = 1;
+                    if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+                    return;
+                }
+                // merge the NC warp states; lane owns channels [lane*E, lane*E + E)
+                constexpr int E = D / 32;
+                RegPartial<D> seg;
+                float mx = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < C::NC; ++w) mx = fmaxf(mx, buf[w * (D + 4) + D]);
-            for (int d = threadIdx.x; d < D + 1; d += C::NC * 32) {
-                float sum = 0.f;
+                for (int w = 0; w < C::NC; ++w) mx = fmaxf(mx, buf[w * (D + 4) + D]);
+                float sz = 0.f;
+#pragma unroll
+                for (int e = 0; e < E; ++e) seg.a[e] = 0.f;
 #pragma unroll
                 for (int w = 0; w < C::NC; ++w) {
                     const float mw = buf[w * (D + 4) + D];
                     const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
-                    sum += (d < D ? buf[w * (D + 4) + d] : buf[w * (D + 4) + D + 1]) * f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) seg.a[e] += buf[w * (D + 4) + lane * E + e] * f;
+                    sz += buf[w * (D + 4) + D + 1] * f;
                 }
-                if (d < D) dst[d] = sum;
-                else {
-                    dst[D] = mx;
-                    dst[D + 1] = sum;
+                seg.mv = mx;
+                seg.zv = sz;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&red_free[par]);
+                const uint32_t row = m0.x, row_segs = m1.w;
+                if (args.finish && row_segs == 1) {
+                    finish_out(row, 1u, seg);
+                } else {
+                    float* dst = partials + (uint64_t)seg_slot * (D + 4);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) dst[lane * E + e] = seg.a[e];
+                    if (lane == 0) {
+                        dst[D] = mx;
+                        dst[D + 1] = sz;
+                    }
+                    if (args.finish) {
+                        // publish the partial and count it; the CTA that counts the
+                        // row's last segment merges all of them
+                        __threadfence();
+                        __syncwarp();
+                        uint32_t done = 0;
+                        if (lane == 0) done = atomicAdd(row_cnt + row, 1u) + 1u;
+                        done = __shfl_sync(0xffffffffu, done, 0);
+                        if (done == row_segs) {
+                            __threadfence();
+                            finish_out(row, row_segs,
+                                       GlobalPartials<D, true>{partials + (uint64_t)__ldg(row_seg + row) * (D + 4)});
+                            if (lane == 0) row_cnt[row] = 0u;  // zero again for the next call
+                        }
+                    }
                 }
             }
             ++seg_count;
@@ -723,79 +902,21 @@ struct CombineArgs {
     uint32_t rows;
 };
 
-template <typename T>
-__device__ __forceinline__ float ldq(const T* p, uint64_t i);
-template <>
-__device__ __forceinline__ float ldq<float>(const float* p, uint64_t i) {
-    return p[i];
-}
-template <>
-__device__ __forceinline__ float ldq<__nv_bfloat16>(const __nv_bfloat16* p, uint64_t i) {
-    return __bfloat162float(p[i]);
-}
-
-template <typename O>
-__device__ __forceinline__ void st_out(O* p, uint64_t i, float v);
-template <>
-__device__ __forceinline__ void st_out<float>(float* p, uint64_t i, float v) {
-    p[i] = v;
-}
-template <>
-__device__ __forceinline__ void st_out<__nv_bfloat16>(__nv_bfloat16* p, uint64_t i, float v) {
-    p[i] = __float2bfloat16_rn(v);
-}
-
-// One warp per row; lane l owns channels [l*E, l*E+E), E = D/32.
+// One warp per row (fixed-split plans): the log-sum-exp merge of the row's
+// partials and, in reference mode, the scratch token.
 template <int D, typename QT, typename OT>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
     pdl_wait_primary();
-    constexpr int E = D / 32;
     const int lane = threadIdx.x & 31;
     const uint32_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (r >= a.rows) return;
     const uint32_t* row_len = reinterpret_cast<const uint32_t*>(a.ws + a.l.row_len);
     const uint32_t* row_seg = reinterpret_cast<const uint32_t*>(a.ws + a.l.row_seg);
     const float* partials = reinterpret_cast<const float*>(a.ws + a.l.partials);
-    OT* out = reinterpret_cast<OT*>(a.out) + (uint64_t)r * D;
-    if (row_len[r] == kInvalidRow) {
-#pragma unroll
-        for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, __uint_as_float(0x7fc00000u));
-        return;
-    }
     const uint32_t s0 = row_seg[r], s1 = row_seg[r + 1];
-    float mx = -INFINITY;
-    for (uint32_t s = s0; s < s1; ++s) mx = fmaxf(mx, partials[(uint64_t)s * (D + 4) + D]);
-    float ms = -INFINITY;
-    if (a.sk) {
-        const QT* q = reinterpret_cast<const QT*>(a.q) + (uint64_t)r * D;
-        float dot = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) dot += (ldq<QT>(q, lane * E + e) * a.scale_log2) * a.sk[(uint64_t)r * D + lane * E + e];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        ms = dot;
-        mx = fmaxf(mx, ms);
-    }
-    float acc[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = 0.f;
-    float z = 0.f;
-    for (uint32_t s = s0; s < s1; ++s) {
-        const float* p = partials + (uint64_t)s * (D + 4);
-        const float m = p[D];
-        const float f = m == -INFINITY ? 0.f : fast_exp2(m - mx);
-        z += p[D + 1] * f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] += p[lane * E + e] * f;
-    }
-    if (a.sk) {
-        const float f = fast_exp2(ms - mx);
-        z += f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] += a.sv[(uint64_t)r * D + lane * E + e] * f;
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, z > 0.f ? acc[e] / z : __uint_as_float(0x7fc00000u));
+    finish_row<D, QT, OT>(lane, r, s1 - s0, row_len[r] == kInvalidRow,
+                          GlobalPartials<D, false>{partials + (uint64_t)s0 * (D + 4)}, a.q, a.sk, a.sv, a.scale_log2,
+                          a.out);
 }
 
 template <int D, typename QT>
@@ -811,6 +932,11 @@ cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
     args.vs_mis = L.vs_mis;
     args.scale_log2 = L.scale_log2;
     args.status = L.status;
+    args.finish = L.split == 0 ? 1u : 0u;
+    args.out_bf16 = L.out_dtype == PP_DTYPE_BF16 ? 1u : 0u;
+    args.out = L.out;
+    args.sk = L.scratch_k;
+    args.sv = L.scratch_v;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(L.max_ctas);
     cfg.blockDim = dim3(C::THREADS);

@@ -190,6 +190,20 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torc
     return out
 
 
+def plan_ragged(k: torch.Tensor, v: torch.Tensor, ks: torch.Tensor, vs: torch.Tensor, lengths: torch.Tensor,
+                heads: int, workspace: torch.Tensor, *, split_tokens: int = 0, scratch: bool = False) -> None:
+    """Writes the attention plan for `lengths` into `workspace`, so that the
+    decode_attention calls of a step that share these lengths (one per layer)
+    can pass plan_ready=True with the same workspace and skip re-planning
+    (the reuse DecodeMetadataCache does, decode_metadata.rs:39-142).
+    `scratch` marks reference-mode calls (a scratch token after the history)."""
+    _require_cuda(k, lengths, workspace)
+    arena = arena_struct(k, v, ks, vs, heads)
+    params = attn_params(split_tokens=split_tokens)
+    N.check(N.lib.pp_b200_plan_ragged(C.byref(arena), C.byref(params), _ptr(lengths), 1 if scratch else 0,
+                                      _ptr(workspace), workspace.numel(), _stream(lengths)))
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torch.Tensor, vs: torch.Tensor,
               sk: torch.Tensor, sv: torch.Tensor, past: torch.Tensor, heads: int, split_tokens: int) -> torch.Tensor:
     """int8_kv_ops::attention (int8_kv_ops.rs:42-55): reference-mode fused attention.

@@ -219,6 +219,31 @@ def test_plan_reuse_across_layers(pp, oracle, cuda):
         np.testing.assert_allclose(host(out), ref, rtol=0, atol=2e-5)
 
 
+def test_repeated_calls_on_one_plan_are_bit_identical(pp, oracle, cuda):
+    """Rows split over several CTAs are merged by the CTA that finishes them
+    last, counted in the workspace; the count must be back at zero after every
+    call, so the same call repeated on one plan gives the same bits."""
+    ops = pp.int8_kv_ops
+    branches, heads, d, cap = 24, 16, 128, 2000
+    lens = torch.tensor([2000, 1, 1999, 640, 17, 1500] * 4, dtype=torch.int32, device=cuda)
+    k, v, ks, vs, g = _random_arena(pp, branches, heads, d, cap, cuda, 77)
+    q = torch.randn(branches * heads, d, device=cuda, generator=g).to(torch.bfloat16)
+    first = ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32)
+    arena = ops.arena_struct(k, v, ks, vs, heads)
+    params = ops.attn_params(q_dtype=torch.bfloat16, out_dtype=torch.float32)
+    ws = ops.new_workspace(arena, params, cuda)
+    import ctypes as C
+    pp._native.check(pp._native.lib.pp_b200_plan_ragged(C.byref(arena), C.byref(params), ops._ptr(lens), 0,
+                                                         ops._ptr(ws), ws.numel(), ops._stream(lens)))
+    for _ in range(5):
+        again = ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32, workspace=ws,
+                                     plan_ready=True)
+        assert torch.equal(again, first)
+    rows = list(range(0, branches * heads, 7))
+    ref = _oracle_rows(oracle, q, k, v, ks, vs, lens.cpu().numpy(), heads, rows)
+    np.testing.assert_allclose(host(first)[rows], ref, rtol=0, atol=2e-5)
+
+
 def test_prepare_self_check_passes(pp, cuda):
     pp.int8_kv_ops.prepare(cuda)
 
