@@ -41,6 +41,10 @@ WORKLOADS = {
                  desc="BASELINE config 1: 32 branches x 16 heads x d128, context 4096, 24 layer caches, bf16 q/out"),
     "cfg4": dict(branches=8, heads=16, d=128, ctx=16384, layers=4,
                  desc="BASELINE config 4 shape: 8 branches x 16 heads x d128, context 16384, 4 layer caches"),
+    # ctx: mean initial context (the CPU sample's length); lengths are drawn per branch from U[lo, hi]
+    "cfg2": dict(branches=64, heads=16, d=128, ctx=4224, layers=1, lo=256, hi=8192, max_steps=256,
+                 desc="BASELINE config 2: 64 branches x 16 heads x d128, initial contexts U[256, 8192], per step "
+                      "quantize+append one bf16 N(0, 0.5^2) K/V token per branch, then decode; one layer"),
 }
 
 
@@ -172,6 +176,168 @@ def run_reference_arm(args, w) -> int:
     return 0
 
 
+def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """ragged quantize+append then decode, one layer.
+
+    Per GPU 64 branches with initial contexts drawn from U[256, 8192]
+    (seeded); a step appends one bf16 K/V token per branch (pp_b200_quant_append
+    at each branch's own offset), re-plans the ragged lengths and runs the
+    decode attention over every branch's whole history.  Steps replay the same
+    256 precomputed tokens, so warm-up steps rewrite identical values.
+    Branches are sharded over ranks by LPT on their initial length."""
+    ops, N = pp.int8_kv_ops, pp._native
+    H, D = w["heads"], w["d"]
+    steps = min(args.steps, w["max_steps"])
+    g = np.random.Generator(np.random.PCG64(2))
+    all_lens = g.integers(w["lo"], w["hi"] + 1, w["branches"] * world).astype(np.int64)
+    shards = pp.kv_cache.BranchShards([int(x) for x in all_lens], world, rank)
+    init = all_lens[shards.mine]
+    B = len(init)
+    rows = B * H
+    cap = int(init.max()) + w["max_steps"]
+    arena = pp.kv_cache.Int8KvArena.zeros(B, H, D, cap, dev)
+    tg = torch.Generator(device=dev)
+    tg.manual_seed(2 + rank)
+    arena.k.random_(0, 256, generator=tg)
+    arena.v.random_(0, 256, generator=tg)
+    arena.k_scale.uniform_(0.005, 0.05, generator=tg)
+    arena.v_scale.uniform_(0.005, 0.05, generator=tg)
+    # per step s: append offsets init + s, attention lengths init + s + 1
+    base = torch.tensor(init, dtype=torch.int32, device=dev)
+    offs = torch.stack([base + s for s in range(steps)]).contiguous()
+    lens = (offs + 1).contiguous()
+    k_new = (torch.randn(steps, rows, D, device=dev, generator=tg) * 0.5).to(torch.bfloat16)
+    v_new = (torch.randn(steps, rows, D, device=dev, generator=tg) * 0.5).to(torch.bfloat16)
+    qs = torch.randn(steps, rows, D, device=dev, generator=tg).to(torch.bfloat16)
+    outs = torch.empty(steps, rows, D, dtype=torch.bfloat16, device=dev)
+    a = arena.struct()
+    params = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+    ws = ops.new_workspace(a, params, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    lib = N.lib
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    ws_p, st_p = P(ws), P(status)
+
+    def step(s: int, q=None, kn=None, vn=None, out=None):
+        q = qs[s] if q is None else q
+        kn = k_new[s] if kn is None else kn
+        vn = v_new[s] if vn is None else vn
+        out = outs[s] if out is None else out
+        N.check(lib.pp_b200_quant_append(C.byref(a), P(kn), P(vn), N.DTYPE_BF16, P(offs[s]), 1, st_p, sp))
+        N.check(lib.pp_b200_decode_attention(C.byref(a), C.byref(params), P(q), None, None, P(lens[s]), P(out),
+                                             ws_p, ws.numel(), st_p, sp))
+
+    for s in range(min(args.warmup, steps)):
+        step(s)
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise SystemExit(f"device status after warm-up: {N.status_message(int(status.item()))}")
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if pg is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for s in range(steps):
+            step(s)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = start.elapsed_time(end)
+    ms_step = max_over_ranks(ms_local) / steps
+
+    # bytes: attention reads every branch's whole history once, plus q, out and the append
+    hist = float(sum((init + s + 1).sum() for s in range(steps))) / steps  # mean tokens per branch-row set
+    attn_bytes = hist * H * (2 * D + 8) + rows * D * 2 * 2
+    append_bytes = rows * (2 * D * 2 + 2 * D + 8)
+    per_step = attn_bytes + append_bytes
+    peak, peak_kind = load_peaks()
+    value = world * per_step / (ms_step * 1e-3) / 1e9
+    achieved = per_step / (ms_local / steps * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        q_h = qs.cpu().pin_memory()
+        k_h = k_new.cpu().pin_memory()
+        v_h = v_new.cpu().pin_memory()
+        o_h = torch.empty(outs.shape, dtype=outs.dtype).pin_memory()
+        q_d, k_d, v_d = torch.empty_like(qs[0]), torch.empty_like(k_new[0]), torch.empty_like(v_new[0])
+        o_d = torch.empty_like(outs[0])
+        e_steps = min(steps, 64)
+
+        def e2e_step(s):
+            q_d.copy_(q_h[s], non_blocking=True)
+            k_d.copy_(k_h[s], non_blocking=True)
+            v_d.copy_(v_h[s], non_blocking=True)
+            arena.append(k_d, v_d, offs[s])
+            ops.decode_attention(q_d, arena.k, arena.v, arena.k_scale, arena.v_scale, lens[s], H,
+                                 out_dtype=torch.bfloat16, split_tokens=args.split, workspace=ws, out=o_d)
+            o_h[s].copy_(o_d, non_blocking=True)
+
+        for s in range(min(args.warmup, e_steps)):
+            e2e_step(s)
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for s in range(e_steps):
+            e2e_step(s)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(s0.elapsed_time(s1) / e_steps)
+        e2e = {"value": world * per_step / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": 3 * rows * D * 2, "d2h_bytes_per_step": rows * D * 2, "ms_per_step": e_ms,
+               "tokens_per_s": world * B / (e_ms * 1e-3)}
+
+    if pg is not None:
+        shards.gather(pg, outs[steps - 1].view(B, H, D).contiguous())
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference(w, steps=3, warmup=1, sample_branches=1, threads=os.cpu_count() or 1, budget_s=20.0)
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 KV (bf16-rounded dequant), bf16 K/V in, bf16 q/out, f32 accumulate",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "cfg2", "desc": w["desc"], "branches_per_gpu": B, "heads": H, "head_dim": D,
+                       "capacity": cap, "mean_context": hist / B, "split_tokens": args.split,
+                       "parallelism": f"branch shards x{world} by LPT on context (no collective in the step)",
+                       "l2": "history read per step > 126 MB L2, no flush"},
+            "tokens_per_s": world * B / (ms_step * 1e-3),
+            "percent_of_peak": 100.0 * value / (world * peak),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_step,
+                         "per_launch_ms": ms_local / steps,
+                         "timed": "timed region / steps: append + plan + attention per step (CUDA events)"},
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "gpu_launches": steps * (4 if args.split else 3),  # append, plan, attention (+ combine)
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -207,6 +373,8 @@ def main() -> int:
     pp = importlib.import_module("pop2-bezier_b200")
     ops = pp.int8_kv_ops
     N = pp._native
+    if args.workload == "cfg2":
+        return run_cfg2(args, w, pp, pg, world, rank, local, dev)
 
     # ---- branch shard of this rank (independent branches, no collective)
     total_branches = w["branches"] * world
@@ -343,7 +511,7 @@ def main() -> int:
         shards.gather(pg, per_branch)
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference(w, steps=3, warmup=1, sample_branches=1, threads=os.cpu_count() or 1, budget_s=20.0)
 
     if rank == 0:

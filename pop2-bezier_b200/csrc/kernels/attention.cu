@@ -331,7 +331,7 @@ struct Cfg {
     static constexpr int OFF_VS = OFF_KS + SC_SLOT;
     static constexpr int OFF_Q = OFF_VS + SC_SLOT;
     static constexpr int OFF_META = OFF_Q + Q_BYTES;
-    static constexpr int STAGE_BYTES = ((OFF_META + 32 + 1023) / 1024) * 1024;
+    static constexpr int STAGE_BYTES = ((OFF_META + 64 + 1023) / 1024) * 1024;
     static constexpr int STAGES = D == 128 ? PP_ATTN_STAGES_D128 : PP_ATTN_STAGES_D64;
     static constexpr int STAGE_BOXES = (T + 255) / 256;  // TMA boxes hold at most 256 rows
     static constexpr int STAGE_BOX = T / STAGE_BOXES;    // tokens per whole-stage box
@@ -339,8 +339,15 @@ struct Cfg {
     static constexpr int RED_FLOATS = NC * (D + 4);
     static constexpr int OFF_RED = STAGES * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_RED + 2 * RED_FLOATS * 4;
-    static constexpr int BAR_COUNT = 2 * STAGES + 4;  // full, empty, reduction ready x2, reduction free x2
-    static constexpr int SMEM_BYTES = OFF_BAR + BAR_COUNT * 8 + 16 + 1024;  // + abort flag + base alignment
+    // full, empty, reduction ready x2, reduction free x2, q split ready x QSLOTS
+    static constexpr int QSLOTS = 16;
+    static constexpr int BAR_COUNT = 2 * STAGES + 4 + QSLOTS;
+    // q of the CTA's segments 1 .. QSLOTS-1, scaled and split into three bf16
+    // terms ([term][channel]), prepared at kernel start (slot 0 unused: the
+    // first segment's warps split q themselves rather than wait)
+    static constexpr int QT_BYTES = 3 * D * 2;
+    static constexpr int OFF_QT = ((OFF_BAR + BAR_COUNT * 8 + 16 + 127) / 128) * 128;
+    static constexpr int SMEM_BYTES = OFF_QT + QSLOTS * QT_BYTES + 1024;  // + base alignment
     static_assert(SMEM_BYTES <= 232448, "shared memory budget of one CTA");
     // Tensor-copy destinations in shared memory must be 128-byte aligned, and
     // the swizzled code tiles 1024-byte aligned (stage bases are 1024-aligned).
@@ -354,6 +361,8 @@ struct Cfg {
 
 struct StageMeta {
     uint32_t row, t, nvalid, slot, flags, ks_off, vs_off, row_segs;
+    // the CTA's work, for the consumers' first stage: segment range, rows without segments
+    uint32_t seg_begin, seg_count, n_orphans, pad[5];
 };
 constexpr uint32_t kFirst = 1u, kLast = 2u, kTerm = 4u;
 
@@ -424,7 +433,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     uint64_t* empty = full + C::STAGES;
     uint64_t* red_bar = empty + C::STAGES;  // [2]: all consumer warps' states are in reduction buffer p
     uint64_t* red_free = red_bar + 2;       // [2]: the finishing warp has read reduction buffer p
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(red_free + 2);
+    uint64_t* q_ready = red_free + 2;       // [QSLOTS]: q split of segment k is in its slot
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(q_ready + C::QSLOTS);
     float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -437,6 +447,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         mbar_init(&red_bar[1], C::NC);
         mbar_init(&red_free[0], 1);
         mbar_init(&red_free[1], 1);
+        for (int k = 0; k < C::QSLOTS; ++k) mbar_init(&q_ready[k], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -460,6 +471,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         // ------------------------------------------------------ producer
         if (lane != 0) return;
         const uint32_t n_ctas = hdr->n_ctas;
+        const uint32_t n_orphans = args.finish ? hdr->n_orphans : 0u;
         uint32_t s_begin = 0, s_end = 0;
         if (blockIdx.x < n_ctas) {
             s_begin = cta_seg[blockIdx.x];
@@ -493,6 +505,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 meta->ks_off = args.ks_mis + tok - ksx;
                 meta->vs_off = args.vs_mis + tok - vsx;
                 meta->row_segs = sd.row_segs;
+                meta->seg_begin = s_begin;
+                meta->seg_count = s_end - s_begin;
+                meta->n_orphans = n_orphans;
                 const uint32_t bytes = nbox * C::BOX * D * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 if (n == (uint32_t)C::T) {  // full stage: whole-stage boxes for K and V
@@ -525,6 +540,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             if (mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, kWaitLimitNs)) {
                 StageMeta* meta = reinterpret_cast<StageMeta*>(smem + slot * C::STAGE_BYTES + C::OFF_META);
                 meta->flags = kTerm;
+                meta->seg_begin = s_begin;
+                meta->seg_count = s_end - s_begin;
+                meta->n_orphans = n_orphans;
                 mbar_arrive(&full[slot]);
                 return;
             }
@@ -561,12 +579,42 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         else
             finish_row<D, QT, float>(lane, r, n, invalid, part, args.q, args.sk, args.sv, args.scale_log2, args.out);
     };
-    if (args.finish) {
-        // rows without segments: invalid (NaN) or, in reference mode, the scratch token alone
-        const uint32_t n_orphans = hdr->n_orphans;
-        const uint32_t* orphans = reinterpret_cast<const uint32_t*>(args.ws + args.l.orphans);
-        for (uint32_t k = blockIdx.x * C::NC + warp; k < n_orphans; k += gridDim.x * C::NC)
-            finish_out(orphans[k], 0u, GlobalPartials<D, false>{partials});
+
+    {
+        // The CTA's work, told by the producer with the first stage: prepare what
+        // later segments need (q splits) and write the rows that have no segments.
+        if (!mbar_wait_bounded(&full[0], 0u, abort_flag, kWaitLimitNs)) {
+            *abort_flag = 1;
+            if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+            return;
+        }
+        const uint4 m2w = lds128(smem_addr(smem + C::OFF_META) + 32u);
+        const uint32_t seg_begin = m2w.x, n_pre = min(m2w.y, (uint32_t)C::QSLOTS), n_orphans = m2w.z;
+        for (uint32_t k = 1 + warp; k < n_pre; k += C::NC) {
+            const uint32_t r = segs[seg_begin + k].row;
+            const QT* qr = reinterpret_cast<const QT*>(args.q) + (uint64_t)r * D;
+            __nv_bfloat16* qslot = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_QT + k * C::QT_BYTES);
+#pragma unroll
+            for (int e = 0; e < D / 32; ++e) {
+                const int ch = lane * (D / 32) + e;
+                const float x = ldq<QT>(qr, ch) * args.scale_log2;
+                const __nv_bfloat16 t0 = __float2bfloat16_rn(x);
+                const float r1 = x - __bfloat162float(t0);
+                const __nv_bfloat16 t1 = __float2bfloat16_rn(r1);
+                const __nv_bfloat16 t2 = __float2bfloat16_rn(r1 - __bfloat162float(t1));
+                qslot[ch] = t0;
+                qslot[D + ch] = t1;
+                qslot[2 * D + ch] = t2;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_ready[k]);
+        }
+        if (n_orphans) {
+            // invalid rows (NaN) or, in reference mode, the scratch token alone
+            const uint32_t* orphans = reinterpret_cast<const uint32_t*>(args.ws + args.l.orphans);
+            for (uint32_t k = blockIdx.x * C::NC + warp; k < n_orphans; k += gridDim.x * C::NC)
+                finish_out(orphans[k], 0u, GlobalPartials<D, false>{partials});
+        }
     }
 
     for (uint32_t it = 0;; ++it) {
@@ -585,16 +633,35 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         const uint32_t nvalid = m0.z, seg_slot = m0.w, ks_off = m1.y, vs_off = m1.z;
 
         if (flags & kFirst) {
-            // q row -> three-term bf16 B fragments for channel slice of thread c.
-            constexpr int QN = D / 4;  // channels per thread: [QN*c, QN*c + QN)
-            float qv[QN];
-            load_q_vals<QT>(smem_addr(st + C::OFF_Q), QN * c, QN, qv);
+            // q row -> three-term bf16 B fragments for channel slice of thread c
+            // (channels [D/4 * c, D/4 * c + D/4), term g; zero for g >= 3)
+            if (seg_count > 0 && seg_count < (uint32_t)C::QSLOTS) {
+                if (!mbar_wait_bounded(&q_ready[seg_count], 0u, abort_flag, kWaitLimitNs)) {
+                    *abort_flag = 1;
+                    if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
+                    return;
+                }
+                const uint32_t qt = smem_addr(smem + C::OFF_QT + seg_count * C::QT_BYTES) + (uint32_t)g * (D * 2) +
+                                    (uint32_t)c * (D / 2);
 #pragma unroll
-            for (int i = 0; i < C::NI; ++i) {
-                const float a0 = qv[4 * i] * args.scale_log2, a1 = qv[4 * i + 1] * args.scale_log2;
-                const float a2 = qv[4 * i + 2] * args.scale_log2, a3 = qv[4 * i + 3] * args.scale_log2;
-                qb[i][0] = split_term_pack(a0, a1, g);
-                qb[i][1] = split_term_pack(a2, a3, g);
+                for (int i = 0; i < C::NI; i += 2) {
+                    const uint4 w = g < 3 ? lds128(qt + i * 8) : make_uint4(0u, 0u, 0u, 0u);
+                    qb[i][0] = w.x;
+                    qb[i][1] = w.y;
+                    qb[i + 1][0] = w.z;
+                    qb[i + 1][1] = w.w;
+                }
+            } else {
+                constexpr int QN = D / 4;
+                float qv[QN];
+                load_q_vals<QT>(smem_addr(st + C::OFF_Q), QN * c, QN, qv);
+#pragma unroll
+                for (int i = 0; i < C::NI; ++i) {
+                    const float a0 = qv[4 * i] * args.scale_log2, a1 = qv[4 * i + 1] * args.scale_log2;
+                    const float a2 = qv[4 * i + 2] * args.scale_log2, a3 = qv[4 * i + 3] * args.scale_log2;
+                    qb[i][0] = split_term_pack(a0, a1, g);
+                    qb[i][1] = split_term_pack(a2, a3, g);
+                }
             }
             m2 = -INFINITY;
             zsum = 0.f;

@@ -185,7 +185,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // 2-D tiled tensor load into shared memory, completion signalled on `bar`
-// as transaction bytes.  No multicast.
+// as transaction bytes.  The tile lands in this CTA's shared memory only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                                             int32_t y) {
     asm volatile(
