@@ -53,6 +53,7 @@ extern "C" {
 #define PP_DEV_OFFSET_RANGE 0x2u     /* append offset >= capacity: row not written */
 #define PP_DEV_LENGTH_RANGE 0x4u     /* attention length > capacity: row output is NaN */
 #define PP_DEV_WAIT_TIMEOUT 0x8u     /* a bounded pipeline wait gave up: output undefined */
+#define PP_DEV_POSITION_RANGE 0x10u  /* RoPE position >= max_context: row not written */
 
 /* Geometry of a caller-owned int8 KV arena for one layer, in the reference's
  * batch-arena layout (app/src/model/cache.rs:301-478, int8_cache.rs:326-359):
@@ -202,6 +203,60 @@ int32_t pp_b200_check_write_offsets(const uint64_t* past_lens, uint64_t count, u
  * the reference runs on one device. */
 int32_t pp_b200_sched_partition(const uint64_t* cost, uint32_t n_branches, uint32_t n_shards,
                                 uint32_t* shard_of_branch, uint64_t* shard_cost);
+
+/* ---- decoder step around the int8 KV path (graph_ops.cu / batch.rs) ---- */
+
+/* Geometry of a QKV projection output: rows (batch rows) x [q | k | v], each
+ * heads * head_dim wide, head_dim 64 or 128; dtype PP_DTYPE_BF16 or F32. */
+typedef struct PpQkvRope {
+    uint32_t struct_size;  /* sizeof(PpQkvRope) */
+    uint32_t rows;
+    uint32_t heads;
+    uint32_t head_dim;
+    uint32_t max_context;  /* rows of the cos / sin tables */
+    int32_t dtype;
+    uint32_t reserved[2];
+} PpQkvRope;
+
+/* q/k RMSNorm (eps 1e-6, per-head weights) and interleaved RoPE: replaces
+ * graph_ops::qkv, kernel pp_graph_qkv (app/src/model/graph_ops.rs:144-174,
+ * graph_ops.cu:34-59), with its rounding points, generalised to head_dim 128
+ * and any max_context.  qkv: [rows, 3*heads*head_dim]; params:
+ * [q_norm head_dim | k_norm head_dim | cos max_context*head_dim/2 |
+ * sin max_context*head_dim/2] (the reference's qk_rope_parameters);
+ * positions: device u32 [rows]; out: [3][rows*heads][head_dim] (q, k, v).
+ * status (nullable): PP_DEV_POSITION_RANGE (row not written). */
+int32_t pp_b200_qkv_rope(const PpQkvRope* geometry, const void* qkv, const void* params,
+                         const uint32_t* positions, void* out, uint32_t* status, void* stream);
+
+/* The same, fused with what the int8 decode path does next (batch.rs:143-155,
+ * int8_cache.rs:326-359): the rotated k and the v of each (row, head) are
+ * quantized and appended to `arena` at slot offsets[row] (commit = 0 writes
+ * the partial-query placeholder), q is written as [rows*heads, head_dim] in
+ * the model dtype, and k / v as the f32 scratch [rows*heads, head_dim] that
+ * pp_b200_decode_attention reads in reference mode.  arena: heads and
+ * head_dim as the geometry, arena rows = rows * heads.  status (nullable):
+ * PP_DEV_POSITION_RANGE, PP_DEV_OFFSET_RANGE, PP_DEV_NONFINITE_INPUT. */
+int32_t pp_b200_qkv_rope_append(const PpQkvRope* geometry, const void* qkv, const void* params,
+                                const uint32_t* positions, const PpKvArena* arena,
+                                const uint32_t* offsets, uint32_t commit, void* q_out,
+                                float* scratch_k, float* scratch_v, uint32_t* status, void* stream);
+
+/* SwiGLU: out[r, c] = silu(gate[r, c]) * up[r, c] over in = [rows, 2*hidden]
+ * (gate | up), with the reference's rounding of exp, sum and quotient:
+ * graph_ops::swiglu, kernel pp_graph_swiglu (graph_ops.rs:175-193,
+ * graph_ops.cu:60-74).  dtype PP_DTYPE_BF16 or F32. */
+int32_t pp_b200_swiglu(const void* in, void* out, uint64_t rows, uint32_t hidden, int32_t dtype,
+                       void* stream);
+
+/* RMSNorm of [rows, width]: out = x * rsqrt(mean(x^2) + eps) * weight, the
+ * candle_nn::ops::rms_norm of PrimitiveModel (mod.rs:671,729,746, batch.rs:132).
+ * With residual != NULL, x is first replaced by round(x + residual) (the
+ * residual adds of mod.rs:722,744), which is also written to x_sum when
+ * x_sum != NULL.  dtype PP_DTYPE_BF16 or F32. */
+int32_t pp_b200_rmsnorm(const void* x, const void* residual, void* x_sum, const void* weight,
+                        void* out, uint64_t rows, uint32_t width, float eps, int32_t dtype,
+                        void* stream);
 
 /* On-device self-check run before int8 caches are created: replaces
  * int8_kv_ops::prepare (int8_kv_ops.rs:57-103) and is called where

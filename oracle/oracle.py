@@ -1,4 +1,4 @@
-"""ctypes binding of the CPU oracle (oracle/int8kv_oracle.c).
+"""ctypes binding of the CPU oracle (oracle/int8kv_oracle.c, oracle/graph_oracle.c).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
 CPU-baseline / reference arm of bench.py.  The product never imports this.
@@ -38,6 +38,12 @@ def lib() -> C.CDLL:
         L.oracle_quant_append.argtypes = [vp, vp, u32, u32, u32, u32, vp, i32, vp, vp, vp, vp]
         L.oracle_max_threads.restype = i32
         L.oracle_max_threads.argtypes = []
+        L.oracle_qkv_rope.restype = i32
+        L.oracle_qkv_rope.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, i32]
+        L.oracle_swiglu.restype = i32
+        L.oracle_swiglu.argtypes = [vp, vp, u64, u32, i32]
+        L.oracle_rmsnorm.restype = i32
+        L.oracle_rmsnorm.argtypes = [vp, vp, vp, vp, vp, u64, u32, f32, i32]
         _lib = L
     return _lib
 
@@ -134,3 +140,39 @@ def quant_append(xk, xv, heads: int, offsets, commit: bool, k_arena, v_arena, ks
 
 def max_threads() -> int:
     return int(lib().oracle_max_threads())
+
+
+# ---------------------------------------------------------------- decoder step
+# Model-dtype arrays are passed as uint16 bf16 bits (bf=True) or float32.
+
+def _model(a, bf: bool) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint16 if bf else np.float32)
+
+
+def qkv_rope(qkv, params, positions, rows: int, heads: int, dim: int, max_context: int, bf: bool) -> np.ndarray:
+    """graph_ops.cu pp_graph_qkv restated: returns planes [3, rows*heads, dim]
+    (rows whose position is outside the table stay zero)."""
+    qkv, params = _model(qkv, bf), _model(params, bf)
+    pos = np.ascontiguousarray(positions, dtype=np.uint32)
+    out = np.zeros((3, rows * heads, dim), dtype=np.uint16 if bf else np.float32)
+    if lib().oracle_qkv_rope(_p(qkv), _p(params), _p(pos), _p(out), rows, heads, dim, max_context, int(bf)):
+        raise ValueError("oracle qkv_rope: unsupported head dim")
+    return out
+
+
+def swiglu(x, rows: int, hidden: int, bf: bool) -> np.ndarray:
+    x = _model(x, bf)
+    out = np.empty((rows, hidden), dtype=np.uint16 if bf else np.float32)
+    lib().oracle_swiglu(_p(x), _p(out), rows, hidden, int(bf))
+    return out
+
+
+def rmsnorm(x, weight, rows: int, width: int, eps: float, bf: bool, residual=None):
+    """Returns (out, x_sum); x_sum is None without a residual."""
+    x, w = _model(x, bf), _model(weight, bf)
+    r = None if residual is None else _model(residual, bf)
+    dt = np.uint16 if bf else np.float32
+    out = np.empty((rows, width), dtype=dt)
+    xs = None if r is None else np.empty((rows, width), dtype=dt)
+    lib().oracle_rmsnorm(_p(x), _p(r), _p(xs), _p(w), _p(out), rows, width, eps, int(bf))
+    return out, xs

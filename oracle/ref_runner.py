@@ -97,3 +97,47 @@ class RefInt8Kernels:
                       C.c_uint32(splits)])
         self._launch("pp_i8_merge", (rows, 1), 64, 0, [partial, out, C.c_uint32(splits)])
         return out.reshape(rows, 1, 64)
+
+
+GRAPH_CUBIN = os.path.join(HERE, "_ref", "graph_ops_ref.cubin")
+
+
+class RefGraphKernels(RefInt8Kernels):
+    """pp_graph_qkv / pp_graph_swiglu with the launch geometry of
+    graph_ops.rs:355-395 (QKV: one 32-thread block per (row, head);
+    element kernels: 1024-thread blocks over the elements)."""
+
+    def __init__(self, cubin: str = GRAPH_CUBIN):
+        torch.cuda.init()
+        torch.empty(1, device="cuda")
+        self.d = _Driver()
+        with open(cubin, "rb") as f:
+            self._image = f.read()
+        self._buf = C.create_string_buffer(self._image, len(self._image))
+        self.mod = C.c_void_p()
+        self.d.check(self.d.cu.cuModuleLoadData(C.byref(self.mod), C.cast(self._buf, C.c_void_p)), "cuModuleLoadData")
+        self.fn = {}
+        for name in ("pp_graph_qkv", "pp_graph_swiglu"):
+            f = C.c_void_p()
+            self.d.check(self.d.cu.cuModuleGetFunction(C.byref(f), self.mod, name.encode()), name)
+            self.fn[name] = f
+
+    def qkv(self, qkv: torch.Tensor, params: torch.Tensor, positions: torch.Tensor, heads: int, dim: int,
+            max_context: int) -> torch.Tensor:
+        rows = qkv.shape[0]
+        bf = qkv.dtype == torch.bfloat16
+        out = torch.zeros(3 * rows * heads * dim, dtype=qkv.dtype, device=qkv.device)
+        self._launch("pp_graph_qkv", (rows * heads, 1), 32, 0,
+                     [qkv, params, positions, out, C.c_uint32(rows), C.c_uint32(heads), C.c_uint32(dim),
+                      C.c_uint32(max_context), C.c_uint32(1 if bf else 0)])
+        return out.reshape(3, rows * heads, dim)
+
+    def swiglu(self, x: torch.Tensor) -> torch.Tensor:
+        rows, cols = x.shape
+        hidden = cols // 2
+        bf = x.dtype == torch.bfloat16
+        out = torch.empty(rows, hidden, dtype=x.dtype, device=x.device)
+        n = rows * hidden
+        self._launch("pp_graph_swiglu", ((n + 1023) // 1024, 1), 1024, 0,
+                     [x, out, C.c_uint32(rows), C.c_uint32(hidden), C.c_uint32(1 if bf else 0)])
+        return out

@@ -23,6 +23,7 @@ DEV_NONFINITE_INPUT = 0x1
 DEV_OFFSET_RANGE = 0x2
 DEV_LENGTH_RANGE = 0x4
 DEV_WAIT_TIMEOUT = 0x8
+DEV_POSITION_RANGE = 0x10
 
 ATTN_PLAN_READY = 0x1
 
@@ -43,6 +44,10 @@ EXPORTED = (
     "pp_b200_checked_batch_rows",
     "pp_b200_check_write_offsets",
     "pp_b200_sched_partition",
+    "pp_b200_qkv_rope",
+    "pp_b200_qkv_rope_append",
+    "pp_b200_swiglu",
+    "pp_b200_rmsnorm",
     "pp_b200_prepare",
 )
 
@@ -72,6 +77,18 @@ class PpAttnParams(C.Structure):
         ("flags", C.c_uint32),
         ("max_ctas", C.c_uint32),
         ("reserved", C.c_uint32),
+    ]
+
+
+class PpQkvRope(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("rows", C.c_uint32),
+        ("heads", C.c_uint32),
+        ("head_dim", C.c_uint32),
+        ("max_context", C.c_uint32),
+        ("dtype", C.c_int32),
+        ("reserved", C.c_uint32 * 2),
     ]
 
 
@@ -110,6 +127,10 @@ def _load() -> C.CDLL:
         "pp_b200_checked_batch_rows": (i32, [u64, u32, P(u64)]),
         "pp_b200_check_write_offsets": (i32, [P(u64), u64, u32, u32, u32]),
         "pp_b200_sched_partition": (i32, [P(u64), u32, u32, P(u32), P(u64)]),
+        "pp_b200_qkv_rope": (i32, [P(PpQkvRope), vp, vp, vp, vp, vp, vp]),
+        "pp_b200_qkv_rope_append": (i32, [P(PpQkvRope), vp, vp, vp, P(PpKvArena), vp, u32, vp, vp, vp, vp, vp]),
+        "pp_b200_swiglu": (i32, [vp, vp, u64, u32, i32, vp]),
+        "pp_b200_rmsnorm": (i32, [vp, vp, vp, vp, vp, u64, u32, C.c_float, i32, vp]),
         "pp_b200_prepare": (i32, [i32]),
     }
     for name, (res, args) in sig.items():

@@ -28,11 +28,12 @@ SOURCES = [
     ("csrc/kernels/quant.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
     ("csrc/kernels/attention.cu", []),
     ("csrc/kernels/attention_static.cu", []),
+    ("csrc/kernels/decoder.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
     ("csrc/host/abi.cpp", []),
     ("csrc/host/sched.cpp", []),
     ("csrc/host/selfcheck.cpp", []),
 ]
-HEADERS = ["csrc/kernels/common.cuh", "csrc/host/internal.h"]
+HEADERS = ["csrc/kernels/common.cuh", "csrc/kernels/quant_row.cuh", "csrc/host/internal.h"]
 
 
 def nvcc() -> str:

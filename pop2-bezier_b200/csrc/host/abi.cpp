@@ -332,12 +332,120 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     return PP_STATUS_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+int32_t check_qkv(const PpQkvRope* g, const void* qkv, const void* params, const uint32_t* positions, const void* out,
+                  const char* what, PpQkvRope& e) {
+    if (!g || g->struct_size < sizeof(PpQkvRope)) return fail(PP_STATUS_PRECONDITION, "%s: PpQkvRope missing", what);
+    e = *g;
+    if (e.rows == 0 || e.heads == 0 || (e.head_dim != 64 && e.head_dim != 128) || e.max_context == 0)
+        return fail(PP_STATUS_PRECONDITION, "graph QKV/RoPE geometry differs: rows=%u heads=%u head_dim=%u max_context=%u",
+                    e.rows, e.heads, e.head_dim, e.max_context);
+    if ((uint64_t)e.rows * e.heads > 0xffffffffull || 3ull * e.heads * e.head_dim > 0xffffffffull)
+        return fail(PP_STATUS_PRECONDITION, "graph metadata exceeds U32 indexing");
+    int32_t s;
+    if ((s = check_dtype(e.dtype, what))) return s;
+    if (!qkv || !params || !positions || !out) return fail(PP_STATUS_PRECONDITION, "%s: NULL pointer", what);
+    return PP_STATUS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t pp_b200_qkv_rope(const PpQkvRope* geometry, const void* qkv, const void* params, const uint32_t* positions,
+                         void* out, uint32_t* status, void* stream) {
+    PpQkvRope g;
+    int32_t s;
+    if ((s = check_qkv(geometry, qkv, params, positions, out, "qkv_rope", g))) return s;
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    pp::QkvRopeLaunch L{};
+    L.qkv = qkv;
+    L.params = params;
+    L.positions = positions;
+    L.rows = g.rows;
+    L.heads = g.heads;
+    L.head_dim = g.head_dim;
+    L.max_context = g.max_context;
+    L.bf16 = g.dtype == PP_DTYPE_BF16;
+    L.out = out;
+    L.status = status;
+    cudaError_t e = pp::launch_qkv_rope(L, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "graph QKV launch");
+}
+
+int32_t pp_b200_qkv_rope_append(const PpQkvRope* geometry, const void* qkv, const void* params,
+                                const uint32_t* positions, const PpKvArena* arena, const uint32_t* offsets,
+                                uint32_t commit, void* q_out, float* scratch_k, float* scratch_v, uint32_t* status,
+                                void* stream) {
+    PpQkvRope g;
+    int32_t s;
+    if ((s = check_qkv(geometry, qkv, params, positions, q_out, "qkv_rope_append", g))) return s;
+    if ((s = check_arena(arena, "qkv_rope_append"))) return s;
+    if (arena->heads != g.heads || arena->head_dim != g.head_dim || (uint64_t)arena->rows != (uint64_t)g.rows * g.heads)
+        return fail(PP_STATUS_PRECONDITION,
+                    "INT8 batch requires [B,H,1,D] scratch and matching row histories: arena %ux%u/%u vs qkv %ux%u/%u",
+                    arena->rows, arena->heads, arena->head_dim, g.rows, g.heads, g.head_dim);
+    if (!offsets || !scratch_k || !scratch_v) return fail(PP_STATUS_PRECONDITION, "qkv_rope_append: NULL pointer");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    pp::QkvRopeLaunch L{};
+    L.qkv = qkv;
+    L.params = params;
+    L.positions = positions;
+    L.rows = g.rows;
+    L.heads = g.heads;
+    L.head_dim = g.head_dim;
+    L.max_context = g.max_context;
+    L.bf16 = g.dtype == PP_DTYPE_BF16;
+    L.out = q_out;
+    L.scratch_k = scratch_k;
+    L.scratch_v = scratch_v;
+    L.arena = arena;
+    L.offsets = offsets;
+    L.commit = commit;
+    L.status = status;
+    cudaError_t e = pp::launch_qkv_rope(L, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "graph QKV append launch");
+}
+
+int32_t pp_b200_swiglu(const void* in, void* out, uint64_t rows, uint32_t hidden, int32_t dtype, void* stream) {
+    int32_t s;
+    if (rows == 0 || hidden == 0) return fail(PP_STATUS_PRECONDITION, "graph operation has an empty dimension");
+    if (rows > UINT64_MAX / (2ull * hidden)) return fail(PP_STATUS_PRECONDITION, "graph operation element count overflow");
+    if ((s = check_dtype(dtype, "swiglu"))) return s;
+    if (!in || !out) return fail(PP_STATUS_PRECONDITION, "swiglu: NULL pointer");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_swiglu(in, out, rows, hidden, dtype == PP_DTYPE_BF16, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "graph SwiGLU launch");
+}
+
+int32_t pp_b200_rmsnorm(const void* x, const void* residual, void* x_sum, const void* weight, void* out, uint64_t rows,
+                        uint32_t width, float eps, int32_t dtype, void* stream) {
+    int32_t s;
+    if (rows == 0 || width == 0 || rows > 0x7fffffffull)
+        return fail(PP_STATUS_PRECONDITION, "rms_norm geometry differs: rows=%llu width=%u", (unsigned long long)rows, width);
+    if (!(eps >= 0.f) || !std::isfinite(eps)) return fail(PP_STATUS_PRECONDITION, "rms_norm eps must be finite and >= 0");
+    if ((s = check_dtype(dtype, "rms_norm"))) return s;
+    if (!x || !weight || !out) return fail(PP_STATUS_PRECONDITION, "rms_norm: NULL pointer");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_rmsnorm(x, residual, x_sum, weight, out, rows, width, eps, dtype == PP_DTYPE_BF16,
+                                       (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "rms_norm launch");
+}
+
 const char* pp_b200_status_message(uint32_t bits) {
     if (bits == 0) return "ok";
     if (bits & PP_DEV_WAIT_TIMEOUT) return "EXECUTION_UNCERTAIN: a bounded device pipeline wait timed out";
     if (bits & PP_DEV_NONFINITE_INPUT) return "non-finite INT8 KV input";
     if (bits & PP_DEV_OFFSET_RANGE) return "batch KV needs context rebuild: append offset outside capacity";
     if (bits & PP_DEV_LENGTH_RANGE) return "INT8 attention lengths differ: length exceeds capacity (row output is NaN)";
+    if (bits & PP_DEV_POSITION_RANGE) return "graph QKV/RoPE position exceeds the RoPE table (row not written)";
     return "unknown device status";
 }
 

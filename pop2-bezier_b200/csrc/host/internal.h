@@ -108,6 +108,26 @@ struct AttnLaunch {
     uint32_t ks_mis, vs_mis;  // element offset of the scale arrays inside their maps
 };
 
+// QKV RoPE (+ int8 append): see decoder.cu.
+struct QkvRopeLaunch {
+    const void* qkv;
+    const void* params;
+    const uint32_t* positions;
+    uint32_t rows, heads, head_dim, max_context;
+    bool bf16;
+    void* out;  // plain: the three planes; fused: q
+    float* scratch_k;
+    float* scratch_v;
+    const PpKvArena* arena;  // NULL: plain
+    const uint32_t* offsets;
+    uint32_t commit;
+    uint32_t* status;
+};
+
+cudaError_t launch_qkv_rope(const QkvRopeLaunch& L, cudaStream_t stream);
+cudaError_t launch_swiglu(const void* in, void* out, uint64_t rows, uint32_t hidden, bool bf, cudaStream_t stream);
+cudaError_t launch_rmsnorm(const void* x, const void* residual, void* x_sum, const void* weight, void* out,
+                           uint64_t rows, uint32_t width, float eps, bool bf, cudaStream_t stream);
 cudaError_t launch_quantize(const void* x, int dtype, uint64_t rows, uint32_t d, uint8_t* packed, float* scales,
                             uint32_t* status, cudaStream_t stream);
 cudaError_t launch_quant_append(const PpKvArena& a, const void* k_new, const void* v_new, int dtype,

@@ -8,6 +8,7 @@
 // This file is compiled without fast-math and with -fmad=false so that every
 // division and product rounds exactly as in the reference.
 #include "common.cuh"
+#include "quant_row.cuh"
 #include "../host/internal.h"
 
 namespace pp {
@@ -30,32 +31,9 @@ template <int D, typename T>
 __device__ __forceinline__ bool quantize_row_warp(const T* x, uint8_t* codes, float* scale_out, int lane) {
     constexpr int E = D / 32;
     float v[E];
-    bool finite = true;
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-        v[e] = load_elem<T>(x, (uint64_t)lane * E + e);
-        finite = finite && isfinite(v[e]);
-    }
-    float m = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) m = fmaxf(m, fabsf(v[e]));
-#pragma unroll
-    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const float s = fmaxf(__fdiv_rn(m, 127.f), 1e-12f);
-    uint32_t packed[(E + 3) / 4] = {};
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        int q = __float2int_rn(__fdiv_rn(v[e], s));
-        q = max(-127, min(127, q));
-        packed[e / 4] |= (uint32_t)(q & 0xff) << (8 * (e % 4));
-    }
-    if constexpr (E == 4) {
-        *reinterpret_cast<uint32_t*>(codes + (uint64_t)lane * 4) = packed[0];
-    } else if constexpr (E == 2) {
-        *reinterpret_cast<uint16_t*>(codes + (uint64_t)lane * 2) = (uint16_t)packed[0];
-    }
-    if (lane == 0) *scale_out = s;
-    return __all_sync(0xffffffffu, finite);
+    for (int e = 0; e < E; ++e) v[e] = load_elem<T>(x, (uint64_t)lane * E + e);
+    return quantize_vals_warp<E>(v, codes, scale_out, lane);
 }
 
 template <int D, typename T>

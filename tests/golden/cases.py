@@ -127,3 +127,52 @@ def cfg0_case(seed: int = 0) -> dict:
     v = g.standard_normal((16, 1024, 64), dtype=np.float32)
     q = g.standard_normal((16, 64), dtype=np.float32)
     return dict(k=k, v=v, q=q)
+
+
+# ------------------------------------------------------------- decoder step
+# Inputs for the reference's pp_graph_qkv / pp_graph_swiglu (graph_ops.cu) and
+# the matching oracle and CUDA functions.  Model-dtype arrays are float32
+# values that are exactly representable in bf16 (so the f32 and bf16 runs see
+# the same numbers); bf16 runs pass their bits.
+
+def rope_tables(max_context: int, dim: int) -> tuple[np.ndarray, np.ndarray]:
+    """cos/sin [max_context, dim/2] in f32 as PrimitiveModel builds them
+    (mod.rs:322-330): inv = 1 / 10000^(2p/dim), angle = pos * inv."""
+    pair = np.arange(dim // 2, dtype=np.float32)
+    inv = (np.float32(1.0) / np.power(np.float32(10000.0), (pair * np.float32(2.0)) / np.float32(dim))).astype(np.float32)
+    pos = np.arange(max_context, dtype=np.float32)[:, None]
+    ang = (pos * inv[None, :]).astype(np.float32)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def bf16_exact(x: np.ndarray) -> np.ndarray:
+    return bf16_to_f32(to_bf16_bits(np.asarray(x, dtype=np.float32)))
+
+
+def qkv_case(seed: int, rows: int, heads: int, dim: int, max_context: int) -> dict:
+    """QKV projection output [rows, 3*heads*dim], the parameter block
+    [q_norm | k_norm | cos | sin] and positions, all bf16-exact."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    qkv = bf16_exact(g.standard_normal((rows, 3 * heads * dim)).astype(np.float32) * np.float32(2.5))
+    qn = bf16_exact(1.0 + 0.2 * g.standard_normal(dim).astype(np.float32))
+    kn = bf16_exact(1.0 + 0.2 * g.standard_normal(dim).astype(np.float32))
+    cos, sin = rope_tables(max_context, dim)
+    params = np.concatenate([qn, kn, bf16_exact(cos).ravel(), bf16_exact(sin).ravel()]).astype(np.float32)
+    positions = g.integers(0, max_context, rows).astype(np.uint32)
+    positions[0] = 0
+    positions[-1] = max_context - 1
+    return dict(qkv=qkv, params=params, positions=positions)
+
+
+def swiglu_case(seed: int, rows: int, hidden: int) -> np.ndarray:
+    g = np.random.Generator(np.random.PCG64(seed))
+    x = g.standard_normal((rows, 2 * hidden)).astype(np.float32) * np.float32(3.0)
+    x[0, :8] = [0.0, -0.0, 88.0, -88.0, 1e-30, -1e-30, 20.0, -20.0]
+    return bf16_exact(x)
+
+
+QKV_CASES = [  # name, seed, rows, heads, dim (the reference kernel supports 64), max_context
+    ("qkv_a", 31, 5, 4, 64, 96),
+    ("qkv_b", 32, 3, 16, 64, 1024),
+]
+SWIGLU_CASES = [("swiglu_a", 41, 7, 300), ("swiglu_b", 42, 3, 5632)]
