@@ -41,6 +41,10 @@ WORKLOADS = {
                  desc="BASELINE config 1: 32 branches x 16 heads x d128, context 4096, 24 layer caches, bf16 q/out"),
     "cfg4": dict(branches=8, heads=16, d=128, ctx=16384, layers=4,
                  desc="BASELINE config 4 shape: 8 branches x 16 heads x d128, context 16384, 4 layer caches"),
+    # the full synthetic decoder step (per GPU: 16 branches; the box: 128 branches on 8 GPUs)
+    "cfg3": dict(branches=16, heads=16, d=128, ctx=2048, layers=24, width=2048, ffn=5632,
+                 desc="BASELINE config 3: synthetic decoder (24 layers, width 2048, 16x128 heads, SwiGLU 5632, "
+                      "RMSNorm, RoPE 10000, random bf16 weights, int8 KV), 16 branches per GPU at context 2048"),
     # ctx: mean initial context (the CPU sample's length); lengths are drawn per branch from U[lo, hi]
     "cfg2": dict(branches=64, heads=16, d=128, ctx=4224, layers=1, lo=256, hi=8192, max_steps=256,
                  desc="BASELINE config 2: 64 branches x 16 heads x d128, initial contexts U[256, 8192], per step "
@@ -338,6 +342,137 @@ def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
 
 
 
+def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """the whole decode step of a synthetic 1B-class decoder.
+
+    Per GPU 16 branches whose int8 caches already hold 2048 tokens (random
+    codes and scales); a step decodes one token for every branch through all
+    24 layers (RMSNorm, QKV projection, fused q/k RMSNorm + RoPE + int8 append,
+    int8 decode attention over history + the new token, output projection,
+    RMSNorm, gate/up projection, SwiGLU, down projection) and the final
+    RMSNorm.  Projections are cuBLAS GEMMs; the rest are this library's
+    kernels.  Each step appends at the next slot, so the context grows by one
+    token per step.  Branches are independent: no collective in the step."""
+    D = pp.decoder
+    cfg = D.DecoderConfig(layers=w["layers"], width=w["width"], heads=w["heads"], head_dim=w["d"],
+                          ffn_hidden=w["ffn"], max_context=w["ctx"] + args.warmup + args.steps + 8)
+    B, L0 = w["branches"], w["ctx"]
+    steps = args.steps
+    model = D.SyntheticDecoder(cfg, branches=B, capacity=cfg.max_context, device=dev, seed=1234 + rank)
+    model.fill_history(None, seed=99 + rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    n_in = args.warmup + steps
+    xs = (torch.randn(n_in, B, cfg.width, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    past = torch.stack([torch.full((B,), L0 + s, dtype=torch.int32, device=dev) for s in range(n_in)]).contiguous()
+    stream = torch.cuda.current_stream(dev)
+    outs = []
+    for s in range(args.warmup):
+        model.step(xs[s].clone(), past[s])
+    torch.cuda.synchronize()
+    if int(model.status.item()) != 0:
+        raise SystemExit(f"device status after warm-up: {pp._native.status_message(int(model.status.item()))}")
+    work = [xs[args.warmup + s].clone() for s in range(steps)]
+    graph = None
+    if not args.no_graph:
+        # the whole step as one CUDA graph: the history length advances by one per replay
+        past_live = past[args.warmup].clone()
+        graph = model.capture(past_live, advance=True)
+        past_live.copy_(past[args.warmup])
+        torch.cuda.synchronize()
+
+    def run_step(s: int) -> torch.Tensor:
+        if graph is not None:
+            return graph.replay(work[s])
+        return model.step(work[s], past[args.warmup + s])
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if pg is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for s in range(steps):
+            outs.append(run_step(s))
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = start.elapsed_time(end)
+    ms_step = max_over_ranks(ms_local) / steps
+    tokens_per_s = world * B / (ms_step * 1e-3)
+
+    # bytes a step must move: every weight once, every layer's history once, the new K/V
+    rows = B * cfg.heads
+    mean_hist = L0 + args.warmup + (steps - 1) / 2.0
+    kv_bytes = cfg.layers * rows * mean_hist * (2 * cfg.head_dim + 8)
+    per_step = model.weight_bytes() + kv_bytes
+    peak, peak_kind = load_peaks()
+    achieved = per_step / (ms_local / steps * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        x_h = xs[args.warmup:].cpu().pin_memory()
+        o_h = torch.empty((steps, B, cfg.width), dtype=torch.bfloat16).pin_memory()
+        x_d = torch.empty(B, cfg.width, dtype=torch.bfloat16, device=dev)
+        e_steps = min(steps, 20)
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if graph is not None:
+            graph.past.copy_(past[args.warmup])
+        s0.record(stream)
+        for s in range(e_steps):
+            x_d.copy_(x_h[s], non_blocking=True)
+            o_h[s].copy_(graph.replay(x_d) if graph is not None else model.step(x_d, past[args.warmup + s]),
+                         non_blocking=True)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(s0.elapsed_time(s1) / e_steps)
+        e2e = {"value": world * B / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": B * cfg.width * 2,
+               "d2h_bytes_per_step": B * cfg.width * 2, "ms_per_step": e_ms}
+
+    if pg is not None:
+        shards = pp.kv_cache.BranchShards([L0] * (B * world), world, rank)
+        shards.gather(pg, outs[-1].contiguous())
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 weights/activations, int8 KV, f32 accumulate", "data": "synthetic (seeded, random weights)",
+            "config": {"workload": "cfg3", "desc": w["desc"], "branches_per_gpu": B, "layers": cfg.layers,
+                       "width": cfg.width, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn_hidden": cfg.ffn_hidden,
+                       "context": L0, "parameters": cfg.parameters(), "cuda_graph": graph is not None,
+                       "parallelism": f"branch shards x{world}, weights replicated (no collective in the step)",
+                       "l2": "weights 2.5 GB + history 3.3 GB per step, larger than L2; no flush"},
+            "tokens_per_s": tokens_per_s,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_step,
+                         "per_launch_ms": ms_local / steps,
+                         "timed": "whole decode step (weights + int8 history bytes) per step, CUDA events"},
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "gpu_launches": steps * (1 + cfg.layers * 5 + 1),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -349,6 +484,7 @@ def main() -> int:
     ap.add_argument("--split", type=int, default=0, help="fixed split size in tokens (0: automatic)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="cfg3: launch the step eagerly instead of as a CUDA graph")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     if args.layers:
@@ -375,6 +511,8 @@ def main() -> int:
     N = pp._native
     if args.workload == "cfg2":
         return run_cfg2(args, w, pp, pg, world, rank, local, dev)
+    if args.workload == "cfg3":
+        return run_cfg3(args, w, pp, pg, world, rank, local, dev)
 
     # ---- branch shard of this rank (independent branches, no collective)
     total_branches = w["branches"] * world

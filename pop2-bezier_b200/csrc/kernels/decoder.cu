@@ -235,6 +235,74 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* x, const void*
     }
 }
 
+// The same with 8 consecutive elements per thread held in registers (one
+// pass over memory, 16-byte accesses): width = 8 * blockDim.x, 16-byte aligned
+// rows.  Sum of squares per thread in element order, shuffle tree, then warps.
+template <bool BF>
+__device__ __forceinline__ void load8(const void* p, uint64_t i, float (&v)[8]) {
+    if constexpr (BF) {
+        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            v[2 * k] = __uint_as_float(w[k] << 16);
+            v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+        }
+    } else {
+        const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+        const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+
+template <bool BF>
+__device__ __forceinline__ void store8(void* p, uint64_t i, const float (&v)[8]) {
+    if constexpr (BF) {
+        uint4 u;
+        u.x = (uint32_t)bf16_bits(v[0]) | ((uint32_t)bf16_bits(v[1]) << 16);
+        u.y = (uint32_t)bf16_bits(v[2]) | ((uint32_t)bf16_bits(v[3]) << 16);
+        u.z = (uint32_t)bf16_bits(v[4]) | ((uint32_t)bf16_bits(v[5]) << 16);
+        u.w = (uint32_t)bf16_bits(v[6]) | ((uint32_t)bf16_bits(v[7]) << 16);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p) + i) = u;
+    } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const void* x, const void* residual, void* x_sum,
+                                                           const void* weight, void* out, uint32_t width, float eps) {
+    __shared__ float part[32];
+    const uint64_t i = (uint64_t)blockIdx.x * width + threadIdx.x * 8u;
+    float v[8];
+    load8<BF>(x, i, v);
+    if (residual) {
+        float r[8];
+        load8<BF>(residual, i, r);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = rnd<BF>(v[k] + r[k]);
+        if (x_sum) store8<BF>(x_sum, i, v);
+    }
+    float ss = v[0] * v[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) ss = ss + v[k] * v[k];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    const int nw = blockDim.x >> 5;
+    for (int k = 0; k < nw; ++k) tot = tot + part[k];
+    const float scale = rsqrtf(tot / (float)width + eps);
+    float wv[8];
+    load8<BF>(weight, threadIdx.x * 8u, wv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = v[k] * scale * wv[k];
+    store8<BF>(out, i, v);
+}
+
 template <int D, bool BF, bool APPEND>
 cudaError_t launch_qkv_t(const QkvArgs& a, cudaStream_t stream) {
     const uint64_t items = (uint64_t)a.rows * a.heads;
@@ -288,6 +356,14 @@ cudaError_t launch_swiglu(const void* in, void* out, uint64_t rows, uint32_t hid
 
 cudaError_t launch_rmsnorm(const void* x, const void* residual, void* x_sum, const void* weight, void* out,
                            uint64_t rows, uint32_t width, float eps, bool bf, cudaStream_t stream) {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (width % 256 == 0 && width <= 8192 && a16(x) && a16(weight) && a16(out) && (!residual || a16(residual)) &&
+        (!x_sum || a16(x_sum))) {
+        const uint32_t threads = width / 8;
+        if (bf) rmsnorm_vec_kernel<true><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
+        else rmsnorm_vec_kernel<false><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
+        return cudaGetLastError();
+    }
     const uint32_t threads = width >= 256 ? 256 : 32 * ((width + 31) / 32);
     if (bf) rmsnorm_kernel<true><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
     else rmsnorm_kernel<false><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);

@@ -223,6 +223,16 @@ class SyntheticDecoder:
         n = sum(t.numel() * t.element_size() for L in self.layers for t in L.values())
         return n + self.final_norm.numel() * self.final_norm.element_size()
 
+    def capture(self, past: torch.Tensor, advance: bool = True) -> "CapturedStep":
+        """Records one step into a CUDA graph (all launches of the step, cuBLAS
+        included) so that a decode loop costs one graph launch per token.  The
+        graph reads its input from `CapturedStep.x` and the per-branch history
+        length from `past` (a device tensor that stays in place); with
+        `advance`, the graph also adds 1 to `past` after the step, so each
+        replay decodes the next position.  Call once the step has run eagerly
+        (library and cuBLAS set-up happen on first use)."""
+        return CapturedStep(self, past, advance)
+
     def step(self, x: torch.Tensor, past: torch.Tensor, positions: torch.Tensor | None = None) -> torch.Tensor:
         """One decode token for every branch.  x [branches, width] (the input
         embedding), past u32/i32 [branches] (tokens already in each branch's
@@ -250,3 +260,32 @@ class SyntheticDecoder:
             swiglu(gate_up, out=b["act"])
             residual = torch.matmul(b["act"], L["down"].t())
         return rmsnorm(xr, self.final_norm, residual=residual, x_sum=xr, out=b["out"])
+
+
+class CapturedStep:
+    """A SyntheticDecoder step recorded in a CUDA graph (see capture())."""
+
+    def __init__(self, model: SyntheticDecoder, past: torch.Tensor, advance: bool):
+        self.model, self.past = model, past
+        self.x = torch.zeros(model.branches, model.cfg.width, dtype=model.dtype, device=model.device)
+        side = torch.cuda.Stream(device=model.device)
+        side.wait_stream(torch.cuda.current_stream(model.device))
+        with torch.cuda.stream(side):  # warm the capture stream (cuBLAS handles, workspaces)
+            keep = past.clone()
+            model.step(self.x.clone(), past)
+            past.copy_(keep)
+        torch.cuda.current_stream(model.device).wait_stream(side)
+        torch.cuda.synchronize(model.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = model.step(self.x, past)
+            if advance:
+                past.add_(1)
+
+    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        """Runs the step on x (copied into the graph's input first when given);
+        returns the graph's output buffer (overwritten by the next replay)."""
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.out

@@ -121,10 +121,11 @@ def test_qkv_rope_append_reports_out_of_range_slots(pp, cuda):
     assert int(status.item()) & N.DEV_POSITION_RANGE
 
 
-def test_rmsnorm_vs_oracle_and_in_place_residual(pp, oracle, cuda):
+@pytest.mark.parametrize("width", [2048, 200])  # 16-byte vector path and the strided path
+def test_rmsnorm_vs_oracle_and_in_place_residual(pp, oracle, cuda, width):
     D = pp.decoder
     g = np.random.Generator(np.random.PCG64(81))
-    rows, width = 5, 2048
+    rows = 5
     x = K.bf16_exact(g.standard_normal((rows, width)).astype(np.float32) * 2)
     r = K.bf16_exact(g.standard_normal((rows, width)).astype(np.float32))
     w = K.bf16_exact(1 + 0.1 * g.standard_normal(width).astype(np.float32))
@@ -201,3 +202,31 @@ def test_synthetic_decoder_step_matches_torch_restatement(pp, cuda):
     rows = torch.arange(3 * cfg.heads, device=cuda)
     slot = past.repeat_interleave(cfg.heads).long()
     assert all((a.k_scale[rows, slot] != hk[2][rows, slot]).all() for a, hk in zip(m.arenas, hist))
+
+
+def test_captured_step_replays_the_eager_step(pp, cuda):
+    """The step recorded as a CUDA graph gives the eager step's bits, and its
+    history length advances by one per replay."""
+    D = pp.decoder
+    cfg = D.DecoderConfig(layers=2, width=256, heads=2, head_dim=128, ffn_hidden=512, max_context=64)
+    m = D.SyntheticDecoder(cfg, branches=3, capacity=64, device=cuda, seed=8)
+    m.fill_history(None, seed=9)
+    gen = torch.Generator(device=cuda).manual_seed(10)
+    xs = [torch.randn(3, cfg.width, device=cuda, generator=gen).to(torch.bfloat16) for _ in range(3)]
+    start = torch.tensor([5, 0, 30], dtype=torch.int32, device=cuda)
+    snap = [(a.k.clone(), a.v.clone(), a.k_scale.clone(), a.v_scale.clone()) for a in m.arenas]
+    eager = []
+    for i, x in enumerate(xs):
+        eager.append(m.step(x.clone(), start + i).clone())
+    for a, (k, v, ks, vs) in zip(m.arenas, snap):  # back to the history before the eager steps
+        a.k.copy_(k), a.v.copy_(v), a.k_scale.copy_(ks), a.v_scale.copy_(vs)
+    past = start.clone()
+    cap = m.capture(past)
+    past.copy_(start)
+    for a, (k, v, ks, vs) in zip(m.arenas, snap):
+        a.k.copy_(k), a.v.copy_(v), a.k_scale.copy_(ks), a.v_scale.copy_(vs)
+    for i, x in enumerate(xs):
+        got = cap.replay(x)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), eager[i].view(torch.int16)), f"step {i}"
+    assert torch.equal(past, start + 3)
