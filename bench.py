@@ -485,6 +485,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="cfg3: launch the step eagerly instead of as a CUDA graph")
+    ap.add_argument("--no-prefetch", action="store_true", help="never stream history before the previous kernel ends")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     if args.layers:
@@ -540,6 +541,10 @@ def main() -> int:
     params = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
     params_ready = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
                                    plan_ready=True)
+    # layers after the first follow another layer's attention, which writes neither this
+    # layer's history nor the plan: they may stream history while it finishes
+    params_prefetch = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
+                                      plan_ready=True, prefetch_history=not args.no_prefetch)
     ws = ops.new_workspace(arenas[0], params, dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -554,8 +559,8 @@ def main() -> int:
         # lengths are identical across layers in a step: plan once, reuse (DecodeMetadataCache)
         N.check(lib.pp_b200_plan_ragged(arena_refs[0], C.byref(params), lens_p, 0, ws_p, ws.numel(), sp))
         for i in range(layers):
-            N.check(lib.pp_b200_decode_attention(arena_refs[i], C.byref(params_ready), q_ptrs[i], None, None, lens_p,
-                                                 o_ptrs[i], ws_p, ws.numel(), st_p, sp))
+            N.check(lib.pp_b200_decode_attention(arena_refs[i], C.byref(params_prefetch if i else params_ready),
+                                                 q_ptrs[i], None, None, lens_p, o_ptrs[i], ws_p, ws.numel(), st_p, sp))
 
     for _ in range(args.warmup):
         step()
@@ -619,7 +624,8 @@ def main() -> int:
             ops.plan_ragged(k0, v0, ks0, vs0, lengths, H, wsp, split_tokens=args.split)
             for i, (k, v, ks, vs) in enumerate(caches):
                 ops.decode_attention(q_dev[i], k, v, ks, vs, lengths, H, out_dtype=torch.bfloat16,
-                                     split_tokens=args.split, workspace=wsp, plan_ready=True, out=outs[i])
+                                     split_tokens=args.split, workspace=wsp, plan_ready=True, out=outs[i],
+                                     prefetch_history=i > 0 and not args.no_prefetch)
             o_host.copy_(outs, non_blocking=True)
 
         for _ in range(max(1, args.warmup)):

@@ -94,6 +94,15 @@ typedef struct PpAttnParams {
  * as DecodeMetadataCache does, app/src/model/decode_metadata.rs:39-142). */
 #define PP_ATTN_PLAN_READY 0x1u
 
+/* With PP_ATTN_PLAN_READY: the kernel enqueued just before this call on the
+ * stream writes neither this arena's history (the tokens attended from it)
+ * nor the workspace plan; for instance another layer's attention, or
+ * pp_b200_qkv_rope_append in reference mode (it writes slot `past`, after the
+ * history).  The attention then starts streaming history while that kernel
+ * finishes (programmatic dependent launch) and waits for it only before
+ * reading q, the scratch token or anything else it may have written. */
+#define PP_ATTN_PREFETCH_HISTORY 0x2u
+
 uint32_t pp_b200_abi_version(void);
 const char* pp_b200_last_error(void);
 

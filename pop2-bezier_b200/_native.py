@@ -26,6 +26,7 @@ DEV_WAIT_TIMEOUT = 0x8
 DEV_POSITION_RANGE = 0x10
 
 ATTN_PLAN_READY = 0x1
+ATTN_PREFETCH_HISTORY = 0x2
 
 # Every symbol include/pp_b200.h declares; the CPU test suite checks the
 # library exports exactly these.

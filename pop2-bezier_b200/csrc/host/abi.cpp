@@ -198,6 +198,10 @@ int32_t prepare_launch(const PpKvArena* arena, const PpAttnParams* params, const
     L.scratch_v = scratch_v;
     L.layout = pp::ws_layout(arena->rows, arena->capacity, arena->head_dim, L.split, L.max_ctas);
     L.plan_ready = (p.flags & PP_ATTN_PLAN_READY) != 0;
+    L.prefetch = (p.flags & PP_ATTN_PREFETCH_HISTORY) != 0;
+    if (L.prefetch && !L.plan_ready)
+        return fail(PP_STATUS_PRECONDITION, "%s: PP_ATTN_PREFETCH_HISTORY needs PP_ATTN_PLAN_READY (the plan kernel "
+                    "writes what the prefetch reads)", what);
     L.use_pdl = true;
     if (!workspace) return fail(PP_STATUS_PRECONDITION, "%s: workspace is NULL", what);
     if (!aligned(workspace, 256)) return fail(PP_STATUS_PRECONDITION, "%s: workspace must be 256-byte aligned", what);

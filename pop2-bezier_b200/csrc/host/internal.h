@@ -101,6 +101,7 @@ struct AttnLaunch {
     WsLayout layout;
     uint32_t* status;
     bool plan_ready;
+    bool prefetch;  // PP_ATTN_PREFETCH_HISTORY
     bool use_pdl;
     // Tensor maps (host-encoded): K, V codes in 16-token boxes and in
     // whole-stage boxes, and K, V scales.

@@ -377,6 +377,7 @@ struct AttnArgs {
     uint32_t* status;
     // row finish (stream-K plans): outputs, reference-mode scratch token
     uint32_t finish;    // 1: this kernel writes the outputs; 0: the combine kernel does
+    uint32_t prefetch;  // PP_ATTN_PREFETCH_HISTORY: stream history before the previous kernel completes
     uint32_t out_bf16;  // output element type: bf16 (1) or f32 (0)
     void* out;
     const float* sk;
@@ -460,8 +461,17 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         tma_prefetch_desc(&map_vs);
     }
     __syncthreads();
-    pdl_launch_dependents();
-    pdl_wait_primary();  // the plan (previous kernel) is complete and visible
+    // The kernel before this one on the stream may still be running (programmatic
+    // dependent launch).  Without PP_ATTN_PREFETCH_HISTORY every thread waits for
+    // it here.  With it, the producer reads the plan and streams K/V history first
+    // (the caller vouches that kernel writes neither) and waits before loading q;
+    // the consumers wait before reading anything.  Dependents of this kernel are
+    // released only after the wait, so a chain of such launches never lets a
+    // kernel start before the ones two places earlier have completed.
+    if (!args.prefetch) {
+        pdl_wait_primary();
+        pdl_launch_dependents();
+    }
 
     const PlanHeader* hdr = reinterpret_cast<const PlanHeader*>(args.ws);
     const uint32_t* cta_seg = reinterpret_cast<const uint32_t*>(args.ws + args.l.cta_seg);
@@ -480,12 +490,26 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         constexpr uint32_t q_bytes = D * sizeof(QT);
         uint32_t it = 0;
         bool ok = true;
+        // q loads of stages issued before the wait (at most one ring's worth)
+        bool waited = !args.prefetch;
+        uint32_t pend_n = 0, pend_slot[C::STAGES];
+        const unsigned char* pend_src[C::STAGES];
+        auto release_q = [&]() {
+            if (waited) return;
+            pdl_wait_primary();
+            pdl_launch_dependents();
+            waited = true;
+            for (uint32_t i = 0; i < pend_n; ++i)
+                bulk_load(smem + pend_slot[i] * C::STAGE_BYTES + C::OFF_Q, pend_src[i], q_bytes, &full[pend_slot[i]]);
+            pend_n = 0;
+        };
         SegDesc next = s_begin < s_end ? segs[s_begin] : SegDesc{0, 0, 0, 0};
         for (uint32_t s = s_begin; s < s_end && ok; ++s) {
             const SegDesc sd = next;
             if (s + 1 < s_end) next = segs[s + 1];
             for (uint32_t t = sd.t0; t < sd.t1; t += C::T, ++it) {
                 const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
+                if (it == (uint32_t)C::STAGES) release_q();  // the ring is full: q before anything else
                 if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, kWaitLimitNs)) {
                     ok = false;
                     break;
@@ -531,10 +555,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 }
                 if (first) {
                     const unsigned char* qrow = reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * q_bytes;
-                    bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
+                    if (waited) {
+                        bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
+                    } else {
+                        pend_slot[pend_n] = slot;
+                        pend_src[pend_n++] = qrow;
+                    }
                 }
             }
         }
+        release_q();  // fewer stages than the ring holds, or an abort: the q loads still go out
         if (ok) {
             const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
             if (mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, kWaitLimitNs)) {
@@ -559,6 +589,10 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     }
 
     // ---------------------------------------------------------- consumers
+    if (args.prefetch) {
+        pdl_wait_primary();
+        pdl_launch_dependents();
+    }
     const int g = lane >> 2, c = lane & 3;
     uint32_t qb[C::NI][2];
     float acc[C::NJ][4];
@@ -1000,6 +1034,7 @@ cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
     args.scale_log2 = L.scale_log2;
     args.status = L.status;
     args.finish = L.split == 0 ? 1u : 0u;
+    args.prefetch = L.prefetch ? 1u : 0u;
     args.out_bf16 = L.out_dtype == PP_DTYPE_BF16 ? 1u : 0u;
     args.out = L.out;
     args.sk = L.scratch_k;

@@ -75,6 +75,9 @@ template <int D, bool BF, bool APPEND>
 __global__ void __launch_bounds__(32 * kQkvWarps) qkv_rope_kernel(const QkvArgs a) {
     constexpr int E = D / 32;
     __shared__ float sq[kQkvWarps][D], skk[kQkvWarps][D], svv[kQkvWarps][D];
+    // a dependent attention launch may start now and stream history (which this
+    // kernel does not write); it waits for this kernel before reading q/k/v
+    pdl_launch_dependents();
     const int t = threadIdx.x & 31, w = threadIdx.x >> 5;
     const uint32_t headrow = blockIdx.x * kQkvWarps + w;
     if (headrow >= a.rows * a.heads) return;

@@ -172,6 +172,7 @@ class SyntheticDecoder:
     def __init__(self, cfg: DecoderConfig, branches: int, capacity: int, device, seed: int = 0,
                  dtype: torch.dtype = torch.bfloat16):
         self.cfg, self.branches, self.capacity = cfg, branches, capacity
+        self.prefetch = True  # see PP_ATTN_PREFETCH_HISTORY
         self.device = torch.device(device)
         self.dtype = dtype
         g = torch.Generator(device=self.device)
@@ -251,9 +252,12 @@ class SyntheticDecoder:
             qkv = torch.matmul(b["normed"], L["qkv"].t())
             qkv_rope_append(qkv, L["rope"], pos, arena, past, cfg.max_context, q_out=b["q"], scratch_k=b["sk"],
                             scratch_v=b["sv"], status=self.status)
+            # qkv_rope_append writes slot past[b], after the history: the attention may stream
+            # the history while it finishes
             ops.decode_attention(b["q"], arena.k, arena.v, arena.k_scale, arena.v_scale, past, H,
                                  scratch_k=b["sk"], scratch_v=b["sv"], out_dtype=self.dtype,
-                                 workspace=self.workspace, plan_ready=True, status=self.status, out=b["att"])
+                                 workspace=self.workspace, plan_ready=True, status=self.status, out=b["att"],
+                                 prefetch_history=self.prefetch)
             proj = torch.matmul(b["att"].view(self.branches, H * d), L["proj"].t())
             rmsnorm(xr, L["norm2"], residual=proj, x_sum=xr, out=b["normed"])
             gate_up = torch.matmul(b["normed"], L["gate_up"].t())

@@ -125,14 +125,14 @@ def arena_struct(k: torch.Tensor, v: torch.Tensor, ks: torch.Tensor, vs: torch.T
 
 def attn_params(*, split_tokens: int = 0, q_dtype: torch.dtype = torch.float32,
                 out_dtype: torch.dtype = torch.float32, softmax_scale: float = 0.0, plan_ready: bool = False,
-                max_ctas: int = 0) -> N.PpAttnParams:
+                max_ctas: int = 0, prefetch_history: bool = False) -> N.PpAttnParams:
     p = N.PpAttnParams()
     p.struct_size = C.sizeof(N.PpAttnParams)
     p.split_tokens = split_tokens
     p.q_dtype = _F32 if q_dtype == torch.float32 else _BF16
     p.out_dtype = _F32 if out_dtype == torch.float32 else _BF16
     p.softmax_scale = softmax_scale
-    p.flags = N.ATTN_PLAN_READY if plan_ready else 0
+    p.flags = (N.ATTN_PLAN_READY if plan_ready else 0) | (N.ATTN_PREFETCH_HISTORY if prefetch_history else 0)
     p.max_ctas = max_ctas
     return p
 
@@ -150,7 +150,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torc
                      scratch_v: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                      split_tokens: int = 0, softmax_scale: float = 0.0, workspace: torch.Tensor | None = None,
                      plan_ready: bool = False, status: torch.Tensor | None = None,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, prefetch_history: bool = False) -> torch.Tensor:
     """General entry: int8 decode attention over a [rows, capacity, d] arena.
 
     q [rows, d] (or [rows, 1, d]) F32/BF16; lengths int32/uint32 [rows/heads].
@@ -179,7 +179,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torc
     odt = out_dtype or q.dtype
     arena = arena_struct(k, v, ks, vs, heads)
     params = attn_params(split_tokens=split_tokens, q_dtype=q.dtype, out_dtype=odt, softmax_scale=softmax_scale,
-                         plan_ready=plan_ready)
+                         plan_ready=plan_ready, prefetch_history=prefetch_history)
     if workspace is None:
         workspace = new_workspace(arena, params, q.device)
     if out is None:

@@ -244,6 +244,31 @@ def test_repeated_calls_on_one_plan_are_bit_identical(pp, oracle, cuda):
     np.testing.assert_allclose(host(first)[rows], ref, rtol=0, atol=2e-5)
 
 
+def test_prefetch_history_gives_the_same_bits(pp, cuda):
+    """Layers that follow another layer's attention may stream their history
+    before it completes; the outputs must not change."""
+    ops = pp.int8_kv_ops
+    branches, heads, d, cap, layers = 8, 16, 128, 3000, 4
+    lens = torch.tensor([3000, 5, 2999, 1200, 17, 640, 3000, 1], dtype=torch.int32, device=cuda)
+    arenas = [_random_arena(pp, branches, heads, d, cap, cuda, 60 + i) for i in range(layers)]
+    qs = [torch.randn(branches * heads, d, device=cuda, generator=g).to(torch.bfloat16) for (_, _, _, _, g) in arenas]
+    k0, v0, ks0, vs0, _ = arenas[0]
+    ws = ops.new_workspace(ops.arena_struct(k0, v0, ks0, vs0, heads), ops.attn_params(), cuda)
+    ops.plan_ragged(k0, v0, ks0, vs0, lens, heads, ws)
+    runs = []
+    for prefetch in (False, True):
+        outs = []
+        for i, (k, v, ks, vs, _) in enumerate(arenas):
+            outs.append(ops.decode_attention(qs[i], k, v, ks, vs, lens, heads, out_dtype=torch.float32, workspace=ws,
+                                             plan_ready=True, prefetch_history=prefetch and i > 0))
+        torch.cuda.synchronize()
+        runs.append(outs)
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
+    with pytest.raises(pp.PreconditionError):
+        ops.decode_attention(qs[0], k0, v0, ks0, vs0, lens, heads, workspace=ws, prefetch_history=True)
+
+
 def test_prepare_self_check_passes(pp, cuda):
     pp.int8_kv_ops.prepare(cuda)
 

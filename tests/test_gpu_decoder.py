@@ -230,3 +230,17 @@ def test_captured_step_replays_the_eager_step(pp, cuda):
         torch.cuda.synchronize()
         assert torch.equal(got.view(torch.int16), eager[i].view(torch.int16)), f"step {i}"
     assert torch.equal(past, start + 3)
+
+
+def test_decoder_step_without_history_prefetch_gives_the_same_bits(pp, cuda):
+    D = pp.decoder
+    cfg = D.DecoderConfig(layers=2, width=256, heads=2, head_dim=128, ffn_hidden=512, max_context=64)
+    m = D.SyntheticDecoder(cfg, branches=3, capacity=64, device=cuda, seed=11)
+    m.fill_history(None, seed=12)
+    past = torch.tensor([40, 7, 0], dtype=torch.int32, device=cuda)
+    x = torch.randn(3, cfg.width, device=cuda, generator=torch.Generator(device=cuda).manual_seed(13)).to(torch.bfloat16)
+    with_prefetch = m.step(x.clone(), past).clone()
+    m.prefetch = False
+    without = m.step(x.clone(), past).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(with_prefetch.view(torch.int16), without.view(torch.int16))
