@@ -45,6 +45,9 @@ WORKLOADS = {
     "cfg3": dict(branches=16, heads=16, d=128, ctx=2048, layers=24, width=2048, ffn=5632,
                  desc="BASELINE config 3: synthetic decoder (24 layers, width 2048, 16x128 heads, SwiGLU 5632, "
                       "RMSNorm, RoPE 10000, random bf16 weights, int8 KV), 16 branches per GPU at context 2048"),
+    # the prefill path: one layer's whole int8 history back to bf16 (int8_cache.rs:363-371)
+    "prefill": dict(branches=32, heads=16, d=128, ctx=4096, layers=1,
+                    desc="prefill dequant: one cfg1 layer's int8 K and V (512 rows x 4096 x d128) to bf16"),
     # ctx: mean initial context (the CPU sample's length); lengths are drawn per branch from U[lo, hi]
     "cfg2": dict(branches=64, heads=16, d=128, ctx=4224, layers=1, lo=256, hi=8192, max_steps=256,
                  desc="BASELINE config 2: 64 branches x 16 heads x d128, initial contexts U[256, 8192], per step "
@@ -473,6 +476,71 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
 
 
 
+def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """The prefill dequant path: one layer's int8 K and V histories back to
+    bf16 (Int8LayerCache::prefill_prefix, int8_cache.rs:363-371), 1.6 GB of
+    codes, scales and bf16 per step on each GPU; no collective."""
+    ops = pp.int8_kv_ops
+    rows, L, D = w["branches"] * w["heads"], w["ctx"], w["d"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5 + rank)
+    k = torch.randint(0, 256, (rows, L, D), dtype=torch.uint8, device=dev, generator=gen)
+    v = torch.randint(0, 256, (rows, L, D), dtype=torch.uint8, device=dev, generator=gen)
+    ks = torch.rand(rows, L, device=dev, generator=gen) * 0.05
+    vs = torch.rand(rows, L, device=dev, generator=gen) * 0.05
+    kb = torch.empty(rows, L, D, dtype=torch.bfloat16, device=dev)
+    vb = torch.empty_like(kb)
+    lib, N = pp._native.lib, pp._native
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    sp = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def step():
+        for codes, sc, out in ((k, ks, kb), (v, vs, vb)):
+            N.check(lib.pp_b200_dequantize(P(codes), P(sc), rows * L, D, 1, N.DTYPE_BF16, P(out), sp))
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.current_stream(dev)
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_step = float(t.item())
+    per_step = 2 * (rows * L * D * (1 + 2) + rows * L * 4)
+    peak, peak_kind = load_peaks()
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": world * per_step / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 codes -> bf16(i8 * scale)", "data": "synthetic (seeded)",
+            "config": {"workload": "prefill", "desc": w["desc"], "rows": rows, "context": L, "head_dim": D,
+                       "l2": "1.6 GB per step, larger than L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": per_step / (ms_local * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": per_step / (ms_local * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                         "per_launch_bytes": per_step / 2, "per_launch_ms": ms_local / 2,
+                         "timed": "two dequantize calls (K, V) per step, CUDA events"},
+            "clocks": clocks.summary(), "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,6 +582,8 @@ def main() -> int:
         return run_cfg2(args, w, pp, pg, world, rank, local, dev)
     if args.workload == "cfg3":
         return run_cfg3(args, w, pp, pg, world, rank, local, dev)
+    if args.workload == "prefill":
+        return run_prefill(args, w, pp, pg, world, rank, local, dev)
 
     # ---- branch shard of this rank (independent branches, no collective)
     total_branches = w["branches"] * world

@@ -7,6 +7,8 @@
 //   q = clamp(round_half_even(x / s), -127, 127)
 // This file is compiled without fast-math and with -fmad=false so that every
 // division and product rounds exactly as in the reference.
+#include <type_traits>
+
 #include "common.cuh"
 #include "quant_row.cuh"
 #include "../host/internal.h"
@@ -108,6 +110,37 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
     }
 }
 
+// The same over 16-byte groups of codes (16 elements of one row, d % 16 == 0):
+// one 16-byte load of codes, one scale, 16 products, 32 or 64 bytes stored.
+template <typename O>
+__global__ void __launch_bounds__(256) dequantize16_kernel(const uint4* __restrict__ packed,
+                                                           const float* __restrict__ scales, uint64_t groups,
+                                                           uint32_t groups_per_row, int round_bf16, O* __restrict__ out) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < groups; i += stride) {
+        const uint4 w = packed[i];
+        const float s = __ldg(scales + i / groups_per_row);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            v[k] = (float)(int8_t)(words[k / 4] >> (8 * (k % 4))) * s;
+            if (round_bf16) v[k] = bf16_round(v[k]);
+        }
+        if constexpr (std::is_same<O, float>::value) {
+            float4* o = reinterpret_cast<float4*>(out + i * 16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        } else {
+            uint4* o = reinterpret_cast<uint4*>(out + i * 16);
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                o[k] = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                                  pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+        }
+    }
+}
+
 // Row-prefix copy between arenas: block (row, chunk) copies 16-byte vectors of
 // codes and 4-byte scales of the committed prefix.
 __global__ void __launch_bounds__(256) copy_prefix_kernel(const uint8_t* __restrict__ sk, const uint8_t* __restrict__ sv,
@@ -187,6 +220,21 @@ cudaError_t launch_quant_append(const PpKvArena& a, const void* k_new, const voi
 cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, uint64_t rows, uint32_t d, int round_bf16,
                               int out_dtype, void* out, cudaStream_t stream) {
     const uint64_t n = rows * d;
+    const bool vec = d % 16 == 0 && (reinterpret_cast<uintptr_t>(packed) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+    if (vec) {
+        const uint64_t groups = n / 16;
+        const uint64_t blocks = (groups + 255) / 256;
+        const uint32_t grid = (uint32_t)(blocks < 148u * 16u ? blocks : 148u * 16u);
+        if (out_dtype == PP_DTYPE_F32)
+            dequantize16_kernel<float><<<grid, 256, 0, stream>>>(reinterpret_cast<const uint4*>(packed), scales, groups,
+                                                                 d / 16, round_bf16, (float*)out);
+        else
+            dequantize16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(reinterpret_cast<const uint4*>(packed), scales,
+                                                                         groups, d / 16, round_bf16,
+                                                                         (__nv_bfloat16*)out);
+        return cudaGetLastError();
+    }
     uint64_t blocks = (n + 255) / 256;
     const uint32_t grid = (uint32_t)(blocks == 0 ? 1 : (blocks < 148u * 32u ? blocks : 148u * 32u));
     if (out_dtype == PP_DTYPE_F32)

@@ -92,6 +92,25 @@ def test_dequantize_vs_oracle(pp, oracle, cuda, out_dtype, d):
     assert np.array_equal(u32(got), u32(want))
 
 
+def test_dequantize_unaligned_view_and_prefill_shape(pp, oracle, cuda):
+    """The prefill path (int8_cache.rs:363-371 `prefill_prefix`: the whole int8
+    history back to bf16) at a prefill-sized [16, 1024, 64], and the same codes
+    through a 4-byte-offset view, which takes the element-wise kernel."""
+    g = np.random.Generator(np.random.PCG64(6))
+    x = g.standard_normal((16, 1024, 64), dtype=np.float32) * 2
+    codes, scales = oracle.quantize(x)
+    want = oracle.dequantize(codes, scales, True)
+    dc, ds = to_dev(codes, cuda), to_dev(scales, cuda)
+    got = pp.int8_kv_ops.dequantize(dc, ds, torch.bfloat16).float().cpu().numpy()
+    assert np.array_equal(u32(got), u32(want))
+    buf = torch.empty(codes.size + 16, dtype=torch.uint8, device=cuda)
+    view = buf[4:4 + codes.size].view(codes.shape)
+    view.copy_(dc)
+    assert view.data_ptr() % 16 == 4
+    got2 = pp.int8_kv_ops.dequantize(view, ds, torch.bfloat16).float().cpu().numpy()
+    assert np.array_equal(u32(got2), u32(want))
+
+
 def _arena_np(a):
     return (a.k.cpu().numpy(), a.v.cpu().numpy(), a.k_scale.cpu().numpy(), a.v_scale.cpu().numpy())
 
