@@ -267,6 +267,17 @@ int32_t pp_b200_rmsnorm(const void* x, const void* residual, void* x_sum, const 
                         void* out, uint64_t rows, uint32_t width, float eps, int32_t dtype,
                         void* stream);
 
+/* Rényi-entropy truncated sampling with classifier-free guidance, one logical
+ * row per block: replaces fused_sampling::sample, kernel pp_renyi_sample
+ * (app/src/inference/fused_sampling.rs:69-90, renyi_sample.cu), with its
+ * checks and its results.  raw: f32 [batch * guidance, choices] (guidance 2:
+ * conditional then unconditional row); uniforms: f32 [batch] in [0, 1);
+ * bounds: u32 [batch, 2] = (start, count) of the legal window; out: u32
+ * [3, batch] = (token_offset + column, 1 or 0 for the fallback, support). */
+int32_t pp_b200_renyi_sample(const float* raw, const float* uniforms, const uint32_t* bounds, uint32_t* out,
+                             uint32_t batch, uint32_t choices, uint32_t guidance, float alpha, float cfg,
+                             uint32_t token_offset, void* stream);
+
 /* On-device self-check run before int8 caches are created: replaces
  * int8_kv_ops::prepare (int8_kv_ops.rs:57-103) and is called where
  * PrimitiveModel::prepare_int8_kv calls it (int8_policy.rs:29-56).  Runs the

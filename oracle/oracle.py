@@ -1,4 +1,4 @@
-"""ctypes binding of the CPU oracle (oracle/int8kv_oracle.c, oracle/graph_oracle.c).
+"""ctypes binding of the CPU oracle (oracle/int8kv_oracle.c, graph_oracle.c, sample_oracle.c).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
 CPU-baseline / reference arm of bench.py.  The product never imports this.
@@ -42,6 +42,8 @@ def lib() -> C.CDLL:
         L.oracle_qkv_rope.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, i32]
         L.oracle_swiglu.restype = i32
         L.oracle_swiglu.argtypes = [vp, vp, u64, u32, i32]
+        L.oracle_renyi_sample.restype = i32
+        L.oracle_renyi_sample.argtypes = [vp, vp, vp, vp, u32, u32, u32, f32, f32, u32]
         L.oracle_rmsnorm.restype = i32
         L.oracle_rmsnorm.argtypes = [vp, vp, vp, vp, vp, u64, u32, f32, i32]
         _lib = L
@@ -176,3 +178,16 @@ def rmsnorm(x, weight, rows: int, width: int, eps: float, bf: bool, residual=Non
     xs = None if r is None else np.empty((rows, width), dtype=dt)
     lib().oracle_rmsnorm(_p(x), _p(r), _p(xs), _p(w), _p(out), rows, width, eps, int(bf))
     return out, xs
+
+
+def renyi_sample(raw, uniforms, bounds, guidance: int, alpha: float, cfg: float, offset: int) -> np.ndarray:
+    """The reference's fused Rényi sampler restated: raw f32 [batch*guidance,
+    choices], uniforms f32 [batch], bounds u32 [batch, 2] -> u32 [3, batch]."""
+    raw = np.ascontiguousarray(raw, dtype=np.float32)
+    u = np.ascontiguousarray(uniforms, dtype=np.float32).reshape(-1)
+    b = np.ascontiguousarray(bounds, dtype=np.uint32).reshape(-1, 2)
+    batch, choices = b.shape[0], raw.shape[1]
+    out = np.zeros((3, batch), dtype=np.uint32)
+    if lib().oracle_renyi_sample(_p(raw), _p(u), _p(b), _p(out), batch, choices, guidance, alpha, cfg, offset):
+        raise ValueError("oracle renyi_sample: unsupported geometry")
+    return out

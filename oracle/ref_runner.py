@@ -141,3 +141,36 @@ class RefGraphKernels(RefInt8Kernels):
         self._launch("pp_graph_swiglu", ((n + 1023) // 1024, 1), 1024, 0,
                      [x, out, C.c_uint32(rows), C.c_uint32(hidden), C.c_uint32(1 if bf else 0)])
         return out
+
+
+RENYI_CUBIN = os.path.join(HERE, "_ref", "renyi_ref.cubin")
+
+
+class RefRenyiKernel(RefInt8Kernels):
+    """pp_renyi_sample with the launch of fused_sampling.rs:147-162 (one
+    256-thread block per logical row, padded * 8 + 256 * 16 shared bytes)."""
+
+    def __init__(self, cubin: str = RENYI_CUBIN):
+        torch.cuda.init()
+        torch.empty(1, device="cuda")
+        self.d = _Driver()
+        with open(cubin, "rb") as f:
+            self._image = f.read()
+        self._buf = C.create_string_buffer(self._image, len(self._image))
+        self.mod = C.c_void_p()
+        self.d.check(self.d.cu.cuModuleLoadData(C.byref(self.mod), C.cast(self._buf, C.c_void_p)), "cuModuleLoadData")
+        f = C.c_void_p()
+        self.d.check(self.d.cu.cuModuleGetFunction(C.byref(f), self.mod, b"pp_renyi_sample"), "pp_renyi_sample")
+        self.fn = {"pp_renyi_sample": f}
+
+    def sample(self, raw: torch.Tensor, uniforms: torch.Tensor, bounds: torch.Tensor, guidance: int, alpha: float,
+               cfg: float, offset: int) -> torch.Tensor:
+        batch, choices = bounds.shape[0], raw.shape[1]
+        padded = 1
+        while padded < choices:
+            padded <<= 1
+        out = torch.zeros(3 * batch, dtype=torch.int32, device=raw.device)
+        self._launch("pp_renyi_sample", (batch, 1), 256, padded * 8 + 256 * 16,
+                     [raw, uniforms, bounds, out, C.c_uint32(batch), C.c_uint32(choices), C.c_uint32(guidance),
+                      C.c_float(alpha), C.c_float(cfg), C.c_uint32(offset), C.c_uint32(padded)])
+        return out.reshape(3, batch)

@@ -9,6 +9,7 @@ from . import _native  # noqa: F401  (loads libpp_b200.so or raises)
 from . import int8_kv_ops  # noqa: F401
 from . import kv_cache  # noqa: F401
 from . import decoder  # noqa: F401
+from . import sampling  # noqa: F401
 from ._native import (  # noqa: F401
     ExecutionUncertainError,
     InvalidOutputError,
@@ -16,5 +17,5 @@ from ._native import (  # noqa: F401
     abi_version,
 )
 
-__all__ = ["int8_kv_ops", "kv_cache", "decoder", "abi_version", "PreconditionError", "InvalidOutputError",
+__all__ = ["int8_kv_ops", "kv_cache", "decoder", "sampling", "abi_version", "PreconditionError", "InvalidOutputError",
            "ExecutionUncertainError"]

@@ -49,6 +49,7 @@ EXPORTED = (
     "pp_b200_qkv_rope_append",
     "pp_b200_swiglu",
     "pp_b200_rmsnorm",
+    "pp_b200_renyi_sample",
     "pp_b200_prepare",
 )
 
@@ -132,6 +133,7 @@ def _load() -> C.CDLL:
         "pp_b200_qkv_rope_append": (i32, [P(PpQkvRope), vp, vp, vp, P(PpKvArena), vp, u32, vp, vp, vp, vp, vp]),
         "pp_b200_swiglu": (i32, [vp, vp, u64, u32, i32, vp]),
         "pp_b200_rmsnorm": (i32, [vp, vp, vp, vp, vp, u64, u32, C.c_float, i32, vp]),
+        "pp_b200_renyi_sample": (i32, [vp, vp, vp, vp, u32, u32, u32, C.c_float, C.c_float, u32, vp]),
         "pp_b200_prepare": (i32, [i32]),
     }
     for name, (res, args) in sig.items():

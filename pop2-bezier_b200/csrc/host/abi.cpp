@@ -443,6 +443,28 @@ int32_t pp_b200_rmsnorm(const void* x, const void* residual, void* x_sum, const 
     return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "rms_norm launch");
 }
 
+int32_t pp_b200_renyi_sample(const float* raw, const float* uniforms, const uint32_t* bounds, uint32_t* out,
+                             uint32_t batch, uint32_t choices, uint32_t guidance, float alpha, float cfg,
+                             uint32_t token_offset, void* stream) {
+    int32_t s;
+    // the checks of fused_sampling.rs:17-67 `validate`
+    if ((guidance != 1 && guidance != 2) || batch == 0 || choices == 0 || choices > 2048)
+        return fail(PP_STATUS_PRECONDITION,
+                    "fused sampler needs 1/2 guidance rows and a nonempty head of at most 2048 choices");
+    if (batch > 0x7fffffffu) return fail(PP_STATUS_PRECONDITION, "fused sampler logical row, uniform or bounds shape mismatch");
+    if (!std::isfinite(alpha) || alpha <= 1.f || !std::isfinite(cfg) || cfg < 0.f || (guidance == 1 && cfg != 1.f))
+        return fail(PP_STATUS_PRECONDITION, "invalid fused sampler alpha/CFG/guidance combination");
+    if ((uint64_t)token_offset + (choices - 1) > 0xffffffffull) return fail(PP_STATUS_PRECONDITION, "fused token range overflow");
+    if (!raw || !uniforms || !bounds || !out) return fail(PP_STATUS_PRECONDITION, "fused sampler: NULL pointer");
+    if (!aligned(raw, 4) || !aligned(uniforms, 4) || !aligned(bounds, 4) || !aligned(out, 4))
+        return fail(PP_STATUS_PRECONDITION, "fused sampler inputs must be 4-byte aligned");
+    DeviceInfo d;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_renyi_sample(raw, uniforms, bounds, out, batch, choices, guidance, alpha, cfg,
+                                            token_offset, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "fused sampler launch");
+}
+
 const char* pp_b200_status_message(uint32_t bits) {
     if (bits == 0) return "ok";
     if (bits & PP_DEV_WAIT_TIMEOUT) return "EXECUTION_UNCERTAIN: a bounded device pipeline wait timed out";

@@ -129,6 +129,9 @@ cudaError_t launch_qkv_rope(const QkvRopeLaunch& L, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* in, void* out, uint64_t rows, uint32_t hidden, bool bf, cudaStream_t stream);
 cudaError_t launch_rmsnorm(const void* x, const void* residual, void* x_sum, const void* weight, void* out,
                            uint64_t rows, uint32_t width, float eps, bool bf, cudaStream_t stream);
+cudaError_t launch_renyi_sample(const float* raw, const float* uniforms, const uint32_t* bounds, uint32_t* out,
+                                uint32_t batch, uint32_t choices, uint32_t guidance, float alpha, float cfg,
+                                uint32_t token_offset, cudaStream_t stream);
 cudaError_t launch_quantize(const void* x, int dtype, uint64_t rows, uint32_t d, uint8_t* packed, float* scales,
                             uint32_t* status, cudaStream_t stream);
 cudaError_t launch_quant_append(const PpKvArena& a, const void* k_new, const void* v_new, int dtype,

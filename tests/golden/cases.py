@@ -176,3 +176,37 @@ QKV_CASES = [  # name, seed, rows, heads, dim (the reference kernel supports 64)
     ("qkv_b", 32, 3, 16, 64, 1024),
 ]
 SWIGLU_CASES = [("swiglu_a", 41, 7, 300), ("swiglu_b", 42, 3, 5632)]
+
+
+# ---------------------------------------------------------------- sampling
+# Inputs for the reference's fused Rényi sampler (renyi_sample.cu): name, seed,
+# batch, choices, guidance, alpha, cfg, token offset.  Each case mixes legal
+# windows, peaky and flat heads, ties and the invalid rows the kernel falls
+# back on (bad uniform, empty or out-of-range window, non-finite logits).
+RENYI_CASES = [
+    ("renyi_a", 51, 12, 270, 1, 4.0, 1.0, 100),
+    ("renyi_b", 52, 9, 2048, 2, 3.5, 2.5, 2048),
+    ("renyi_c", 53, 8, 17, 2, 1.5, 0.0, 0),
+]
+
+
+def renyi_case(seed: int, batch: int, choices: int, guidance: int) -> dict:
+    g = np.random.Generator(np.random.PCG64(seed))
+    raw = (g.standard_normal((batch * guidance, choices)) * 2.0).astype(np.float32)
+    uniforms = g.uniform(0.0, 1.0, batch).astype(np.float32)
+    starts = g.integers(0, choices // 2, batch).astype(np.uint32)
+    counts = np.maximum(1, g.integers(1, choices - starts + 1)).astype(np.uint32)
+    bounds = np.stack([starts, counts], 1).astype(np.uint32)
+    rg = lambda r: slice(r * guidance, (r + 1) * guidance)  # noqa: E731
+    raw[rg(0)] *= 8.0                      # peaky head: support 1
+    raw[rg(1)] *= 0.0                      # flat head: support = count, ties broken by column
+    uniforms[1] = np.float32(0.999)
+    uniforms[2] = np.float32(0.0)          # rank 0: the arg-max path
+    bounds[3] = (0, choices)               # the whole head
+    uniforms[4] = np.float32(1.0)          # invalid uniform
+    bounds[5] = (choices, 1)               # window outside the head
+    if batch > 6:
+        raw[rg(6)][0, choices // 3] = np.float32(np.nan)  # non-finite logit: fallback
+    if batch > 7:
+        bounds[7] = (1, 0)                 # empty window
+    return dict(raw=raw, uniforms=uniforms, bounds=bounds)
