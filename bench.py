@@ -1,6 +1,6 @@
 """Benchmark of the int8 historical-KV decode step on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg2|cfg3|cfg4|prefill|float]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1, one rank per GPU)
 
 Workload cfg1 (the one the headline metric is quoted
@@ -48,6 +48,10 @@ WORKLOADS = {
     # the prefill path: one layer's whole int8 history back to bf16 (int8_cache.rs:363-371)
     "prefill": dict(branches=32, heads=16, d=128, ctx=4096, layers=1,
                     desc="prefill dequant: one cfg1 layer's int8 K and V (512 rows x 4096 x d128) to bf16"),
+    # the float-KV path (fused_attention.rs): bf16 K/V at the reference kernel's head_dim 64, f32 q/out
+    "float": dict(branches=32, heads=16, d=64, ctx=4096, layers=24, kv="bf16",
+                  desc="float-KV decode attention: 32 branches x 16 heads x d64, bf16 K/V, context 4096, "
+                       "24 layer caches, f32 q/out (the reference's F32 query and output)"),
     # ctx: mean initial context (the CPU sample's length); lengths are drawn per branch from U[lo, hi]
     "cfg2": dict(branches=64, heads=16, d=128, ctx=4224, layers=1, lo=256, hi=8192, max_steps=256,
                  desc="BASELINE config 2: 64 branches x 16 heads x d128, initial contexts U[256, 8192], per step "
@@ -160,18 +164,54 @@ def cpu_reference(w, steps: int, warmup: int, sample_branches: int, threads: int
                       f"per step, {len(times)} timed steps, oracle/int8kv_oracle.c (reference arithmetic restated)"}
 
 
+def cpu_float_reference(w, steps: int, warmup: int, sample_branches: int, threads: int, budget_s: float) -> dict:
+    """The float-KV attention arithmetic restated on the CPU
+    (oracle/float_attn_oracle.c), timed on a bounded sample: `sample_branches`
+    branches of one layer per step, all host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    rows, L, D = sample_branches * w["heads"], w["ctx"], w["d"]
+    g = np.random.Generator(np.random.PCG64(1))
+    k = g.standard_normal((rows, L, D), dtype=np.float32)
+    v = g.standard_normal((rows, L, D), dtype=np.float32)
+    if w.get("kv", "bf16") == "bf16":
+        k = (k.view(np.uint32) >> 16).astype(np.uint16)
+        v = (v.view(np.uint32) >> 16).astype(np.uint16)
+    q = g.standard_normal((rows, D), dtype=np.float32)
+    elem = 2 if w.get("kv", "bf16") == "bf16" else 4
+    per_call = rows * L * 2 * D * elem + rows * D * 8
+    for _ in range(max(0, warmup)):
+        oracle.float_attention(q, k, v, None, w["heads"], threads=threads)
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        oracle.float_attention(q, k, v, None, w["heads"], threads=threads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    mean = sum(times) / len(times)
+    return {"value": per_call / mean / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_branches} branches x {w['heads']} heads x ctx {L} x d{D} {w.get('kv', 'bf16')} K/V of "
+                      f"one layer per step, {len(times)} timed steps, oracle/float_attn_oracle.c (the reference "
+                      f"kernel's arithmetic restated)"}
+
+
 def run_reference_arm(args, w) -> int:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    cb = cpu_reference(w, args.steps, args.warmup, sample_branches=1, threads=threads, budget_s=120.0)
+    ref = cpu_float_reference if args.workload == "float" else cpu_reference
+    cb = ref(w, args.steps, args.warmup, sample_branches=1, threads=threads, budget_s=120.0)
     n = args.gpus
     line = {
         "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
         "impl": "reference", "value": cb["value"], "unit": "GB/s", "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 KV, f32 accumulate", "data": "synthetic (seeded)",
+        "dtype": ("bf16 KV" if args.workload == "float" else "int8 KV") + ", f32 accumulate",
+        "data": "synthetic (seeded)",
         "config": {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"],
                    "heads": w["heads"], "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"],
                    "parallelism": "replicas only (host cores)"},
@@ -541,6 +581,147 @@ def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
 
 
 
+def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """The float-KV decode path (fused_attention::decode_attention): per step
+    one plan, then one pp_b200_decode_attention_float per layer cache; branch
+    shards per rank as the int8 path, no collective in the step."""
+    fa, ops, N = pp.fused_attention, pp.int8_kv_ops, pp._native
+    B, H, D, L, layers = w["branches"], w["heads"], w["d"], w["ctx"], w["layers"]
+    rows = B * H
+    kv_t = torch.bfloat16 if w.get("kv", "bf16") == "bf16" else torch.float32
+    elem = 2 if kv_t == torch.bfloat16 else 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    caches = [(torch.randn(rows, L, D, device=dev, generator=gen).to(kv_t),
+               torch.randn(rows, L, D, device=dev, generator=gen).to(kv_t)) for _ in range(layers)]
+    lengths = torch.full((B,), L, dtype=torch.int32, device=dev)
+    qs = torch.randn(layers, rows, D, device=dev, generator=gen)
+    outs = torch.empty(layers, rows, D, device=dev)
+    kvs = [fa.kv_struct(k, v, H) for k, v in caches]
+    params = ops.attn_params(split_tokens=args.split)
+    p_ready = ops.attn_params(split_tokens=args.split, plan_ready=True)
+    p_pref = ops.attn_params(split_tokens=args.split, plan_ready=True, prefetch_history=not args.no_prefetch)
+    ws = torch.empty(fa.workspace_bytes(kvs[0], params), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp, lib = C.c_void_p(stream.cuda_stream), N.lib
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    lens_p, ws_p, st_p = P(lengths), P(ws), P(status)
+    q_ptrs = [P(qs[i]) for i in range(layers)]
+    o_ptrs = [P(outs[i]) for i in range(layers)]
+    kv_refs = [C.byref(g) for g in kvs]
+
+    def step():
+        N.check(lib.pp_b200_plan_ragged_float(kv_refs[0], C.byref(params), lens_p, ws_p, ws.numel(), sp))
+        for i in range(layers):
+            N.check(lib.pp_b200_decode_attention_float(kv_refs[i], C.byref(p_pref if i else p_ready), q_ptrs[i], D,
+                                                       lens_p, o_ptrs[i], ws_p, ws.numel(), st_p, sp))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise SystemExit(f"device status after warm-up: {N.status_message(int(status.item()))}")
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if pg is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = e0.elapsed_time(e1)
+    ms_step = max_over_ranks(ms_local) / args.steps
+    call_ms = ms_local / (args.steps * layers)
+    per_call = rows * L * 2 * D * elem + rows * D * 4 + rows * D * 4
+    peak, peak_kind = load_peaks()
+
+    e2e = None
+    if not args.no_e2e:
+        q_host = qs.cpu().pin_memory()
+        o_host = torch.empty(outs.shape, dtype=outs.dtype).pin_memory()
+        q_dev = torch.empty_like(qs)
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            fa.plan_ragged(caches[0][0], caches[0][1], lengths, H, ws, split_tokens=args.split)
+            for i, (k, v) in enumerate(caches):
+                fa.decode_attention(q_dev[i].unsqueeze(1), k, v, lengths, H, args.split, workspace=ws,
+                                    plan_ready=True, prefetch_history=i > 0 and not args.no_prefetch,
+                                    out=outs[i].unsqueeze(1))
+            o_host.copy_(outs, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        e_steps = max(1, min(args.steps, 50))
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(s0.elapsed_time(s1) / e_steps)
+        e2e = {"value": world * layers * per_call / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
+               "d2h_bytes_per_step": o_host.numel() * o_host.element_size(), "ms_per_step": e_ms,
+               "tokens_per_s": world * B / (e_ms * 1e-3)}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_float_reference(w, steps=3, warmup=1, sample_branches=1, threads=os.cpu_count() or 1,
+                                  budget_s=20.0)
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                traffic = json.load(f).get("float")
+        except Exception:
+            traffic = None
+    if rank == 0:
+        value = world * layers * per_call / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": f"{w.get('kv', 'bf16')} KV, f32 q/out, f32 accumulate", "data": "synthetic (seeded)",
+            "config": {"workload": "float", "desc": w["desc"], "branches_per_gpu": B, "heads": H, "head_dim": D,
+                       "context": L, "layers": layers, "kv_dtype": w.get("kv", "bf16"), "split_tokens": args.split,
+                       "parallelism": f"branch shards x{world} (no collective in the step)",
+                       "l2": "inputs larger than L2 (each layer cache > 126 MB), no flush"},
+            "tokens_per_s": world * B / (ms_step * 1e-3),
+            "percent_of_peak": 100.0 * value / (world * peak),
+            "roofline": {"bound": "hbm", "achieved": per_call / (call_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": per_call / (call_ms * 1e-3) / 1e9 / peak, "traffic": traffic,
+                         "peak_kind": peak_kind, "per_launch_bytes": per_call, "per_launch_ms": call_ms,
+                         "timed": "timed region / attention calls (CUDA events on the launching stream): "
+                                  "attn_kernel over float rows, with the plan amortised over the step"},
+            "clocks": clocks.summary(), "e2e": e2e,
+            "gpu_launches": args.steps * (1 + (2 if args.split else 1) * layers),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -554,10 +735,13 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="cfg3: launch the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-prefetch", action="store_true", help="never stream history before the previous kernel ends")
+    ap.add_argument("--kv-dtype", choices=["bf16", "f32"], default=None, help="float workload: K/V element type")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     if args.layers:
         w["layers"] = args.layers
+    if args.kv_dtype:
+        w["kv"] = args.kv_dtype
     if args.impl == "reference":
         return run_reference_arm(args, w)
 
@@ -584,6 +768,8 @@ def main() -> int:
         return run_cfg3(args, w, pp, pg, world, rank, local, dev)
     if args.workload == "prefill":
         return run_prefill(args, w, pp, pg, world, rank, local, dev)
+    if args.workload == "float":
+        return run_float(args, w, pp, pg, world, rank, local, dev)
 
     # ---- branch shard of this rank (independent branches, no collective)
     total_branches = w["branches"] * world

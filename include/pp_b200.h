@@ -191,6 +191,58 @@ int32_t pp_b200_decode_attention_static(const PpKvArena* arena, const PpAttnPara
                                         const float* scratch_k, const float* scratch_v,
                                         const uint32_t* lengths, void* out, uint32_t* status, void* stream);
 
+/* Float K/V rows for the float-KV fused decode attention, in the layout the
+ * reference's decode_attention requires (fused_attention.rs:12-23: dense
+ * width and token strides):
+ *   k, v  [rows, tokens, head_dim] of dtype (f32 or bf16); token stride
+ *         head_dim elements, row strides k_row_stride / v_row_stride elements
+ * Row r = branch * heads + head.  k and v must be 16-byte aligned and the
+ * row strides multiples of 16 bytes (the tensor copies' rule); a view of a
+ * larger cache (row stride = capacity * head_dim) is accepted as is. */
+typedef struct PpFloatKv {
+    uint32_t struct_size; /* sizeof(PpFloatKv) */
+    uint32_t rows;        /* physical head rows = branches * heads */
+    uint32_t heads;       /* heads per branch (rows % heads == 0) */
+    uint32_t head_dim;    /* 64 or 128 */
+    uint32_t tokens;      /* key length of every row (the reference's `length` dim) */
+    int32_t dtype;        /* PP_DTYPE_F32 or PP_DTYPE_BF16, both K and V */
+    uint64_t k_row_stride;
+    uint64_t v_row_stride;
+    const void* k;
+    const void* v;
+} PpFloatKv;
+
+/* Workspace bytes pp_b200_decode_attention_float / pp_b200_plan_ragged_float
+ * need for this geometry. */
+size_t pp_b200_float_attention_workspace_size(const PpFloatKv* kv, const PpAttnParams* params);
+
+/* The ragged plan of pp_b200_plan_ragged for float K/V: lengths (device u32
+ * [rows/heads], or NULL for every row attending to all `tokens`) become the
+ * split work list in `workspace`, reusable across layers with
+ * PP_ATTN_PLAN_READY. */
+int32_t pp_b200_plan_ragged_float(const PpFloatKv* kv, const PpAttnParams* params, const uint32_t* lengths,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused float-KV decode attention (QK^T -> softmax -> PV, split-K with a
+ * log-sum-exp combine): replaces fused_attention::decode_attention
+ * (fused_attention.rs:8-83, kernels pp_attention_f32 / pp_attention_bf16 /
+ * pp_attention_merge, decode_attention.cu:7-59).
+ *   q        [rows, head_dim] (params->q_dtype) with row stride q_row_stride
+ *            elements (16-byte aligned rows)
+ *   lengths  device u32 [rows/heads], or NULL: row r attends to its first
+ *            lengths[r / heads] tokens; 0 or > tokens gives NaN (the
+ *            reference's `valid`, decode_attention.cu:14)
+ *   out      [rows, head_dim] (params->out_dtype), dense
+ * Scale 0.125 at head_dim 64 as the reference, f32(1/sqrt(d)) otherwise,
+ * unless params->softmax_scale is set.  params->split_tokens 0 selects the
+ * stream-K plan (balanced over all SMs whatever the raggedness; the reference
+ * keeps each row whole in one CTA); otherwise rows are cut into fixed splits
+ * of clamp(split_tokens, 32, 1024) tokens as fused_attention.rs:29 does.
+ * status (nullable): PP_DEV_LENGTH_RANGE, PP_DEV_WAIT_TIMEOUT. */
+int32_t pp_b200_decode_attention_float(const PpFloatKv* kv, const PpAttnParams* params, const void* q,
+                                       uint64_t q_row_stride, const uint32_t* lengths, void* out, void* workspace,
+                                       size_t workspace_bytes, uint32_t* status, void* stream);
+
 /* Decodes device status bits into a message (static storage). */
 const char* pp_b200_status_message(uint32_t status_bits);
 

@@ -44,6 +44,8 @@ def lib() -> C.CDLL:
         L.oracle_swiglu.argtypes = [vp, vp, u64, u32, i32]
         L.oracle_renyi_sample.restype = i32
         L.oracle_renyi_sample.argtypes = [vp, vp, vp, vp, u32, u32, u32, f32, f32, u32]
+        L.oracle_float_attention.restype = i32
+        L.oracle_float_attention.argtypes = [vp, u64, vp, u64, vp, u64, i32, vp, u32, u32, u32, u32, u32, f32, vp, i32]
         L.oracle_rmsnorm.restype = i32
         L.oracle_rmsnorm.argtypes = [vp, vp, vp, vp, vp, u64, u32, f32, i32]
         _lib = L
@@ -190,4 +192,29 @@ def renyi_sample(raw, uniforms, bounds, guidance: int, alpha: float, cfg: float,
     out = np.zeros((3, batch), dtype=np.uint32)
     if lib().oracle_renyi_sample(_p(raw), _p(u), _p(b), _p(out), batch, choices, guidance, alpha, cfg, offset):
         raise ValueError("oracle renyi_sample: unsupported geometry")
+    return out
+
+
+def float_attention(q, k, v, lengths, heads: int, *, size: int | None = None, split_tokens: int = 0,
+                    scale: float | None = None, threads: int = 1) -> np.ndarray:
+    """Float-KV fused decode attention (float_attn_oracle.c).
+
+    q f32 [rows, q_stride] (first d channels used); k, v [rows, cap, d] f32, or
+    uint16 bf16 bits; only the first `size` tokens of a row exist (default
+    cap); lengths u32 [rows/heads] or None.  Returns f32 [rows, d]."""
+    rows, cap, d = k.shape
+    size = cap if size is None else size
+    if scale is None:
+        scale = 0.125 if d == 64 else float(np.float32(1.0 / np.sqrt(d)))
+    bf = k.dtype == np.uint16
+    if (v.dtype == np.uint16) != bf:
+        raise ValueError("K and V dtypes differ")
+    qc = np.ascontiguousarray(q, dtype=np.float32)
+    kc, vc = np.ascontiguousarray(k), np.ascontiguousarray(v)
+    lens = None if lengths is None else np.ascontiguousarray(lengths, dtype=np.uint32)
+    out = np.empty((rows, d), dtype=np.float32)
+    rc = lib().oracle_float_attention(_p(qc), qc.shape[1], _p(kc), cap * d, _p(vc), cap * d, int(bf), _p(lens),
+                                      rows, heads, d, size, split_tokens, scale, _p(out), threads)
+    if rc:
+        raise ValueError(f"oracle float attention failed ({rc})")
     return out

@@ -174,3 +174,48 @@ class RefRenyiKernel(RefInt8Kernels):
                      [raw, uniforms, bounds, out, C.c_uint32(batch), C.c_uint32(choices), C.c_uint32(guidance),
                       C.c_float(alpha), C.c_float(cfg), C.c_uint32(offset), C.c_uint32(padded)])
         return out.reshape(3, batch)
+
+
+FLOAT_CUBIN = os.path.join(HERE, "_ref", "decode_attention_ref.cubin")
+
+
+class RefFloatAttention(RefInt8Kernels):
+    """pp_attention_f32 / pp_attention_bf16 / pp_attention_merge with the
+    launch of fused_attention.rs:46-83: grid (rows, splits), 128 threads,
+    (split + 128) * 4 shared bytes; partials [rows, splits, 66] and a 64-thread
+    merge when there is more than one split."""
+
+    def __init__(self, cubin: str = FLOAT_CUBIN):
+        torch.cuda.init()
+        torch.empty(1, device="cuda")
+        self.d = _Driver()
+        with open(cubin, "rb") as f:
+            self._image = f.read()
+        self._buf = C.create_string_buffer(self._image, len(self._image))
+        self.mod = C.c_void_p()
+        self.d.check(self.d.cu.cuModuleLoadData(C.byref(self.mod), C.cast(self._buf, C.c_void_p)), "cuModuleLoadData")
+        self.fn = {}
+        for name in ("pp_attention_f32", "pp_attention_bf16", "pp_attention_merge"):
+            f = C.c_void_p()
+            self.d.check(self.d.cu.cuModuleGetFunction(C.byref(f), self.mod, name.encode()), name)
+            self.fn[name] = f
+
+    def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lengths: torch.Tensor | None,
+                  heads: int, split_tokens: int, size: int | None = None) -> torch.Tensor:
+        """q f32 [rows, qs]; k, v [rows, cap, 64] f32 or bf16 (the first `size`
+        tokens are the tensor's key length); lengths int32/uint32 [rows/heads]."""
+        rows, cap, d = k.shape
+        size = cap if size is None else size
+        split = size if split_tokens == 0 else min(max(split_tokens, 32), 1024)
+        splits = (size + split - 1) // split
+        out = torch.empty(rows * 64, dtype=torch.float32, device=q.device)
+        part = torch.empty(rows * splits * 66, dtype=torch.float32, device=q.device) if splits > 1 else None
+        name = "pp_attention_bf16" if k.dtype == torch.bfloat16 else "pp_attention_f32"
+        self._launch(name, (rows, splits), 128, (split + 128) * 4,
+                     [q, k, v, lengths if lengths is not None else C.c_uint64(0), part if part is not None else out,
+                      C.c_uint32(heads), C.c_uint32(size), C.c_uint32(split), C.c_uint32(splits),
+                      C.c_uint32(1 if lengths is not None else 0), C.c_uint64(q.stride(0)), C.c_uint64(cap * d),
+                      C.c_uint64(cap * d)])
+        if part is not None:
+            self._launch("pp_attention_merge", (rows, 1), 64, 0, [part, out, C.c_uint32(splits)])
+        return out.reshape(rows, 64)

@@ -10,6 +10,7 @@ from . import int8_kv_ops  # noqa: F401
 from . import kv_cache  # noqa: F401
 from . import decoder  # noqa: F401
 from . import sampling  # noqa: F401
+from . import fused_attention  # noqa: F401
 from ._native import (  # noqa: F401
     ExecutionUncertainError,
     InvalidOutputError,

@@ -50,6 +50,9 @@ EXPORTED = (
     "pp_b200_swiglu",
     "pp_b200_rmsnorm",
     "pp_b200_renyi_sample",
+    "pp_b200_float_attention_workspace_size",
+    "pp_b200_plan_ragged_float",
+    "pp_b200_decode_attention_float",
     "pp_b200_prepare",
 )
 
@@ -79,6 +82,21 @@ class PpAttnParams(C.Structure):
         ("flags", C.c_uint32),
         ("max_ctas", C.c_uint32),
         ("reserved", C.c_uint32),
+    ]
+
+
+class PpFloatKv(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("rows", C.c_uint32),
+        ("heads", C.c_uint32),
+        ("head_dim", C.c_uint32),
+        ("tokens", C.c_uint32),
+        ("dtype", C.c_int32),
+        ("k_row_stride", C.c_uint64),
+        ("v_row_stride", C.c_uint64),
+        ("k", C.c_void_p),
+        ("v", C.c_void_p),
     ]
 
 
@@ -134,6 +152,9 @@ def _load() -> C.CDLL:
         "pp_b200_swiglu": (i32, [vp, vp, u64, u32, i32, vp]),
         "pp_b200_rmsnorm": (i32, [vp, vp, vp, vp, vp, u64, u32, C.c_float, i32, vp]),
         "pp_b200_renyi_sample": (i32, [vp, vp, vp, vp, u32, u32, u32, C.c_float, C.c_float, u32, vp]),
+        "pp_b200_float_attention_workspace_size": (sz, [P(PpFloatKv), P(PpAttnParams)]),
+        "pp_b200_plan_ragged_float": (i32, [P(PpFloatKv), P(PpAttnParams), vp, vp, sz, vp]),
+        "pp_b200_decode_attention_float": (i32, [P(PpFloatKv), P(PpAttnParams), vp, u64, vp, vp, vp, sz, vp, vp]),
         "pp_b200_prepare": (i32, [i32]),
     }
     for name, (res, args) in sig.items():

@@ -16,11 +16,6 @@
 
 #include "internal.h"
 
-namespace pp {
-uint32_t attention_scale_box_elems();
-uint32_t attention_stage_tokens();
-}
-
 namespace {
 
 thread_local std::string g_last_error;
@@ -166,37 +161,28 @@ int32_t encode_scale_map(CUtensorMap* map, uint32_t* mis, const float* base, con
     return PP_STATUS_OK;
 }
 
-int32_t prepare_launch(const PpKvArena* arena, const PpAttnParams* params, const uint32_t* lengths,
-                       const float* scratch_k, const float* scratch_v, void* workspace, size_t ws_bytes,
-                       pp::AttnLaunch& L, const char* what) {
+// Launch fields shared by the int8 and float entry points: options, device,
+// plan layout and workspace.  `split` is the fixed split (0: stream-K).
+int32_t prepare_common(const PpAttnParams& p, uint32_t split, const uint32_t* lengths, void* workspace,
+                       size_t ws_bytes, pp::AttnLaunch& L, const char* what) {
     int32_t s;
-    if ((s = check_arena(arena, what))) return s;
-    const PpAttnParams p = effective_params(params);
     if ((s = check_dtype(p.q_dtype, "q"))) return s;
     if ((s = check_dtype(p.out_dtype, "out"))) return s;
-    if (!lengths) return fail(PP_STATUS_PRECONDITION, "INT8 attention lengths differ: lengths pointer is NULL");
-    if ((scratch_k == nullptr) != (scratch_v == nullptr))
-        return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be F32[head_rows,1,%u]: pass both or neither", arena->head_dim);
-    if ((scratch_k && !aligned(scratch_k, 4)) || (scratch_v && !aligned(scratch_v, 4)))
-        return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be 4-byte aligned");
     if (!(p.softmax_scale >= 0.f) || !std::isfinite(p.softmax_scale))
         return fail(PP_STATUS_PRECONDITION, "softmax_scale must be finite and >= 0");
     DeviceInfo d;
     if ((s = device_info(d))) return s;
-    L = pp::AttnLaunch{};
-    L.arena = *arena;
-    L.split = p.split_tokens;
+    const uint32_t hd = L.arena.head_dim;
+    L.split = split;
     L.q_dtype = p.q_dtype;
     L.out_dtype = p.out_dtype;
     const float scale = p.softmax_scale > 0.f ? p.softmax_scale
-                                              : (arena->head_dim == 64 ? 0.125f : (float)(1.0 / std::sqrt((double)arena->head_dim)));
+                                              : (hd == 64 ? 0.125f : (float)(1.0 / std::sqrt((double)hd)));
     L.scale_log2 = scale * 1.4426950408889634f;
     L.max_ctas = ctas_for(p, d);
     L.num_sms = (uint32_t)d.num_sms;
     L.lengths = lengths;
-    L.scratch_k = scratch_k;
-    L.scratch_v = scratch_v;
-    L.layout = pp::ws_layout(arena->rows, arena->capacity, arena->head_dim, L.split, L.max_ctas);
+    L.layout = pp::ws_layout(L.arena.rows, L.arena.capacity, hd, L.split, L.max_ctas);
     L.plan_ready = (p.flags & PP_ATTN_PLAN_READY) != 0;
     L.prefetch = (p.flags & PP_ATTN_PREFETCH_HISTORY) != 0;
     if (L.prefetch && !L.plan_ready)
@@ -208,6 +194,87 @@ int32_t prepare_launch(const PpKvArena* arena, const PpAttnParams* params, const
     if (ws_bytes < L.layout.total)
         return fail(PP_STATUS_PRECONDITION, "%s: workspace too small (%zu < %zu bytes)", what, ws_bytes, L.layout.total);
     L.ws = static_cast<unsigned char*>(workspace);
+    return PP_STATUS_OK;
+}
+
+int32_t prepare_launch(const PpKvArena* arena, const PpAttnParams* params, const uint32_t* lengths,
+                       const float* scratch_k, const float* scratch_v, void* workspace, size_t ws_bytes,
+                       pp::AttnLaunch& L, const char* what) {
+    int32_t s;
+    if ((s = check_arena(arena, what))) return s;
+    const PpAttnParams p = effective_params(params);
+    if (!lengths) return fail(PP_STATUS_PRECONDITION, "INT8 attention lengths differ: lengths pointer is NULL");
+    if ((scratch_k == nullptr) != (scratch_v == nullptr))
+        return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be F32[head_rows,1,%u]: pass both or neither", arena->head_dim);
+    if ((scratch_k && !aligned(scratch_k, 4)) || (scratch_v && !aligned(scratch_v, 4)))
+        return fail(PP_STATUS_PRECONDITION, "INT8 scratch must be 4-byte aligned");
+    L = pp::AttnLaunch{};
+    L.arena = *arena;
+    L.kv_kind = pp::kKvInt8;
+    L.q_stride = arena->head_dim;
+    L.scratch_k = scratch_k;
+    L.scratch_v = scratch_v;
+    return prepare_common(p, p.split_tokens, lengths, workspace, ws_bytes, L, what);
+}
+
+// Geometry checks of fused_attention.rs:12-25, plus what the tensor copies need.
+int32_t check_float_kv(const PpFloatKv* kv, const char* what) {
+    if (!kv || kv->struct_size < sizeof(PpFloatKv)) return fail(PP_STATUS_PRECONDITION, "%s: PpFloatKv missing", what);
+    const PpFloatKv& g = *kv;
+    if (g.rows == 0 || g.heads == 0 || g.rows % g.heads != 0 || g.tokens == 0 ||
+        (g.head_dim != 64 && g.head_dim != 128) || (g.dtype != PP_DTYPE_F32 && g.dtype != PP_DTYPE_BF16))
+        return fail(PP_STATUS_PRECONDITION,
+                    "fused decode attention requires F32[batch*heads,1,64|128] and same-device BF16/F32 K/V: "
+                    "rows=%u heads=%u head_dim=%u tokens=%u dtype=%d",
+                    g.rows, g.heads, g.head_dim, g.tokens, g.dtype);
+    if (g.rows > 0x7fffffffu || g.tokens > 0x7fffff00u)
+        return fail(PP_STATUS_PRECONDITION, "fused attention dimensions overflow: rows=%u tokens=%u", g.rows, g.tokens);
+    if (!g.k || !g.v) return fail(PP_STATUS_PRECONDITION, "%s: NULL K/V pointer", what);
+    const uint64_t elem = g.dtype == PP_DTYPE_F32 ? 4 : 2, dense = (uint64_t)g.tokens * g.head_dim;
+    if (g.k_row_stride < dense || g.v_row_stride < dense)
+        return fail(PP_STATUS_PRECONDITION, "fused attention requires dense width and token strides: row strides %llu/%llu "
+                    "< tokens*head_dim=%llu", (unsigned long long)g.k_row_stride, (unsigned long long)g.v_row_stride,
+                    (unsigned long long)dense);
+    if (!aligned(g.k, 16) || !aligned(g.v, 16) || (g.k_row_stride * elem) % 16 || (g.v_row_stride * elem) % 16 ||
+        g.k_row_stride * elem >= (1ull << 40) || g.v_row_stride * elem >= (1ull << 40))
+        return fail(PP_STATUS_PRECONDITION, "fused attention requires dense width and token strides: K/V rows must "
+                    "start on 16-byte boundaries (base and row stride)");
+    return PP_STATUS_OK;
+}
+
+int32_t prepare_float_launch(const PpFloatKv* kv, const PpAttnParams* params, const uint32_t* lengths,
+                             void* workspace, size_t ws_bytes, pp::AttnLaunch& L, const char* what) {
+    int32_t s;
+    if ((s = check_float_kv(kv, what))) return s;
+    const PpAttnParams p = effective_params(params);
+    L = pp::AttnLaunch{};
+    L.arena.struct_size = sizeof(PpKvArena);
+    L.arena.rows = kv->rows;
+    L.arena.heads = kv->heads;
+    L.arena.head_dim = kv->head_dim;
+    L.arena.capacity = kv->tokens;
+    L.kv_kind = kv->dtype == PP_DTYPE_BF16 ? pp::kKvBf16 : pp::kKvF32;
+    L.q_stride = kv->head_dim;
+    // fused_attention.rs:29: split_tokens.clamp(32, 1024), 0 = whole rows
+    const uint32_t split = p.split_tokens == 0 ? 0u : p.split_tokens < 32 ? 32u : p.split_tokens > 1024 ? 1024u
+                                                                                                      : p.split_tokens;
+    return prepare_common(p, split, lengths, workspace, ws_bytes, L, what);
+}
+
+// 3-D map over float K or V rows: dims {head_dim, tokens, rows}, boxes of one
+// 128-byte panel x `box_tokens` tokens, 128-byte swizzle.
+int32_t encode_float_map(CUtensorMap* map, const void* base, uint64_t row_stride, const PpFloatKv& kv,
+                         uint32_t box_tokens) {
+    const uint32_t elem = kv.dtype == PP_DTYPE_F32 ? 4u : 2u;
+    cuuint64_t dims[3] = {kv.head_dim, kv.tokens, kv.rows};
+    cuuint64_t strides[2] = {(cuuint64_t)kv.head_dim * elem, (cuuint64_t)row_stride * elem};
+    cuuint32_t box[3] = {128u / elem, box_tokens, 1u};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PP_STATUS_PRECONDITION, "cuTensorMapEncodeTiled (float K/V) failed: %d", (int)r);
     return PP_STATUS_OK;
 }
 
@@ -333,6 +400,62 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     if ((e = pp::launch_attention(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 attention launch");
     // stream-K plans are finished inside the attention kernel; fixed splits need the combine
     if (L.split && (e = pp::launch_combine(L, st)) != cudaSuccess) return cuda_fail(e, "INT8 combine launch");
+    return PP_STATUS_OK;
+}
+
+size_t pp_b200_float_attention_workspace_size(const PpFloatKv* kv, const PpAttnParams* params) {
+    if (!kv || kv->struct_size < sizeof(PpFloatKv) || kv->rows == 0 || (kv->head_dim != 64 && kv->head_dim != 128))
+        return 0;
+    const PpAttnParams p = effective_params(params);
+    uint32_t g = p.max_ctas;
+    if (!g) {
+        DeviceInfo d;
+        if (device_info(d) != PP_STATUS_OK) g = 1024;  // conservative without a device
+        else g = (uint32_t)d.num_sms;
+    }
+    const uint32_t split = p.split_tokens == 0 ? 0u : p.split_tokens < 32 ? 32u : p.split_tokens > 1024 ? 1024u
+                                                                                                      : p.split_tokens;
+    return pp::ws_layout(kv->rows, kv->tokens, kv->head_dim, split, g).total;
+}
+
+int32_t pp_b200_plan_ragged_float(const PpFloatKv* kv, const PpAttnParams* params, const uint32_t* lengths,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+    pp::AttnLaunch L;
+    int32_t s = prepare_float_launch(kv, params, lengths, workspace, workspace_bytes, L, "plan_ragged_float");
+    if (s) return s;
+    cudaError_t e = pp::launch_plan(L, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "fused attention plan launch");
+}
+
+int32_t pp_b200_decode_attention_float(const PpFloatKv* kv, const PpAttnParams* params, const void* q,
+                                       uint64_t q_row_stride, const uint32_t* lengths, void* out, void* workspace,
+                                       size_t workspace_bytes, uint32_t* status, void* stream) {
+    pp::AttnLaunch L;
+    int32_t s = prepare_float_launch(kv, params, lengths, workspace, workspace_bytes, L, "decode_attention_float");
+    if (s) return s;
+    if (!q || !out)
+        return fail(PP_STATUS_PRECONDITION, "fused decode attention requires F32[batch*heads,1,%u]: NULL q/out",
+                    kv->head_dim);
+    const uint64_t qe = L.q_dtype == PP_DTYPE_F32 ? 4 : 2;
+    if (q_row_stride < kv->head_dim || !aligned(q, 16) || (q_row_stride * qe) % 16)
+        return fail(PP_STATUS_PRECONDITION, "fused attention requires dense width and token strides: q rows must "
+                    "start on 16-byte boundaries (q_row_stride=%llu)", (unsigned long long)q_row_stride);
+    if (!aligned(out, L.out_dtype == PP_DTYPE_F32 ? 4 : 2))
+        return fail(PP_STATUS_PRECONDITION, "decode_attention_float: out is misaligned");
+    L.q = q;
+    L.q_stride = q_row_stride;
+    L.out = out;
+    L.status = status;
+    const uint32_t stage = pp::attention_float_stage_tokens(kv->head_dim, L.kv_kind);
+    if ((s = encode_float_map(&L.map_k, kv->k, kv->k_row_stride, *kv, 16))) return s;
+    if ((s = encode_float_map(&L.map_v, kv->v, kv->v_row_stride, *kv, 16))) return s;
+    if ((s = encode_float_map(&L.map_k_stage, kv->k, kv->k_row_stride, *kv, stage))) return s;
+    if ((s = encode_float_map(&L.map_v_stage, kv->v, kv->v_row_stride, *kv, stage))) return s;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    if (!L.plan_ready && (e = pp::launch_plan(L, st)) != cudaSuccess) return cuda_fail(e, "fused attention plan launch");
+    if ((e = pp::launch_attention(L, st)) != cudaSuccess) return cuda_fail(e, "fused attention launch");
+    if (L.split && (e = pp::launch_combine(L, st)) != cudaSuccess) return cuda_fail(e, "fused attention merge launch");
     return PP_STATUS_OK;
 }
 

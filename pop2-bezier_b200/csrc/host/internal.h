@@ -85,8 +85,15 @@ inline WsLayout ws_layout(uint32_t rows, uint32_t capacity, uint32_t head_dim, u
     return l;
 }
 
+// Element type of the attended K/V (internal codes, not PP_DTYPE_*).
+constexpr int kKvInt8 = 0, kKvBf16 = 1, kKvF32 = 2;
+
 struct AttnLaunch {
+    // int8 arena geometry; for float K/V, capacity is the key length (size)
+    // and k/v/k_scale/v_scale are unused
     PpKvArena arena;
+    int kv_kind;        // kKvInt8, kKvBf16 or kKvF32
+    uint64_t q_stride;  // elements between q rows (head_dim for the int8 entry points)
     uint32_t split;
     int q_dtype, out_dtype;
     float scale_log2;     // softmax scale * log2(e)
@@ -104,7 +111,8 @@ struct AttnLaunch {
     bool prefetch;  // PP_ATTN_PREFETCH_HISTORY
     bool use_pdl;
     // Tensor maps (host-encoded): K, V codes in 16-token boxes and in
-    // whole-stage boxes, and K, V scales.
+    // whole-stage boxes, and K, V scales (int8 only).  Float K/V maps are
+    // 3-D {channel, token, row} with one 128-byte panel per box.
     CUtensorMap map_k, map_v, map_k_stage, map_v_stage, map_ks, map_vs;
     uint32_t ks_mis, vs_mis;  // element offset of the scale arrays inside their maps
 };
@@ -144,6 +152,9 @@ cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t launch_combine(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t configure_attention_kernels(int device);
+uint32_t attention_scale_box_elems();
+uint32_t attention_stage_tokens();
+uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind);
 
 // Records `msg` as the calling thread's last error and returns `status`.
 int32_t fail_msg(int32_t status, const char* msg);

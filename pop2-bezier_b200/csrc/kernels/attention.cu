@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     __syncthreads();
 
     auto history = [&](uint32_t r, bool& valid) -> uint32_t {
-        uint32_t len = __ldg(a.lengths + r / a.heads);
+        uint32_t len = a.lengths ? __ldg(a.lengths + r / a.heads) : a.capacity;  // no lengths: every row is full
         valid = a.scratch ? (len <= a.capacity) : (len > 0 && len <= a.capacity);
         return valid ? len : 0u;
     };
@@ -311,17 +311,31 @@ struct RegPartial {
 #define PP_ATTN_STAGES_D64 4
 #endif
 
-template <int D>
+// Element type of the K/V history: int8 codes with per-token scales (the
+// int8 arena), or plain bf16 / f32 rows (the float-KV cache).
+enum class Kv : int { I8 = kKvInt8, BF16 = kKvBf16, F32 = kKvF32 };
+
+template <int D, Kv KV = Kv::I8>
 struct Cfg {
-    static constexpr int NC = PP_ATTN_NC;           // consumer warps
+    static constexpr bool SCALED = KV == Kv::I8;    // int8 codes + scale arrays
+    static constexpr int ELEM = KV == Kv::I8 ? 1 : KV == Kv::BF16 ? 2 : 4;
+    static constexpr int ROW = D * ELEM;            // bytes of one token of K (or V)
+    // Shared-memory tiles are swizzled panels of at most 128-byte rows: a row
+    // wider than 128 bytes is split into ROW / 128 panels, each a separate
+    // [tokens][128 B] tile, so reads stay bank-conflict free.
+    static constexpr int PANEL = ROW < 128 ? ROW : 128;
+    static constexpr int PANELS = ROW / PANEL;
+    // consumer warps: all 15 while a stage of 240 tokens fits ~62 KB, fewer
+    // (fewer tokens per stage) for the wider float rows
+    static constexpr int NC = ROW <= 128 ? PP_ATTN_NC : ROW == 256 ? 8 : 4;
     static constexpr int THREADS = (NC + 1) * 32;   // + one producer warp
     static constexpr int BOX = 16;                  // tokens per MMA block and per tail TMA box
     static constexpr int NB = PP_ATTN_NB;           // MMA blocks per consumer warp per stage
     static constexpr int TPW = BOX * NB;            // tokens per consumer warp per stage
     static constexpr int T = TPW * NC;              // tokens per stage
-    static constexpr int KV_BYTES = T * D;
+    static constexpr int KV_BYTES = T * ROW;
     static constexpr int SC_BOX = 160;              // scale elements per TMA box (640 B: keeps every box 128B-aligned)
-    static constexpr int SC_BOXES = (T + 4 + SC_BOX - 1) / SC_BOX;  // T tokens + alignment slack
+    static constexpr int SC_BOXES = SCALED ? (T + 4 + SC_BOX - 1) / SC_BOX : 0;  // T tokens + alignment slack
     static constexpr int SC_BYTES = SC_BOXES * SC_BOX * 4;
     static constexpr int Q_BYTES = D * 4;
     static constexpr int OFF_K = 0;
@@ -332,10 +346,11 @@ struct Cfg {
     static constexpr int OFF_Q = OFF_VS + SC_SLOT;
     static constexpr int OFF_META = OFF_Q + Q_BYTES;
     static constexpr int STAGE_BYTES = ((OFF_META + 64 + 1023) / 1024) * 1024;
-    static constexpr int STAGES = D == 128 ? PP_ATTN_STAGES_D128 : PP_ATTN_STAGES_D64;
+    static constexpr int STAGES = !SCALED ? 3 : D == 128 ? PP_ATTN_STAGES_D128 : PP_ATTN_STAGES_D64;
     static constexpr int STAGE_BOXES = (T + 255) / 256;  // TMA boxes hold at most 256 rows
     static constexpr int STAGE_BOX = T / STAGE_BOXES;    // tokens per whole-stage box
     static_assert(STAGE_BOX * STAGE_BOXES == T && STAGE_BOX % BOX == 0, "stage splits into equal boxes");
+    static_assert(SCALED || STAGE_BOXES == 1, "float stages are one box per panel");
     static constexpr int RED_FLOATS = NC * (D + 4);
     static constexpr int OFF_RED = STAGES * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_RED + 2 * RED_FLOATS * 4;
@@ -350,13 +365,38 @@ struct Cfg {
     static constexpr int SMEM_BYTES = OFF_QT + QSLOTS * QT_BYTES + 1024;  // + base alignment
     static_assert(SMEM_BYTES <= 232448, "shared memory budget of one CTA");
     // Tensor-copy destinations in shared memory must be 128-byte aligned, and
-    // the swizzled code tiles 1024-byte aligned (stage bases are 1024-aligned).
+    // the swizzled tiles 1024-byte aligned (stage bases are 1024-aligned).
     static_assert((SC_BOX * 4) % 128 == 0 && OFF_KS % 128 == 0 && OFF_VS % 128 == 0, "scale boxes 128B-aligned");
-    static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && (BOX * D) % 1024 == 0 && (STAGE_BOX * D) % 1024 == 0,
-                  "code boxes 1024B-aligned");
+    static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && (BOX * PANEL) % 1024 == 0 &&
+                      (STAGE_BOX * PANEL) % 1024 == 0 && (T * PANEL) % 1024 == 0,
+                  "tiles 1024B-aligned");
     static_assert(STAGE_BYTES % 1024 == 0 && OFF_Q % 16 == 0 && OFF_META % 16 == 0, "stage layout alignment");
     static constexpr int NI = D / 16;  // q.k MMAs per 16-token block (k = 16 channels each)
     static constexpr int NJ = D / 16;  // p.V MMAs per 16-token block (m = 16 channels each)
+
+    // Channel maps.  In q.k MMA i, thread (g, c) supplies the k positions
+    // 2c, 2c+1, 2c+8, 2c+9, which stand for the four channels from qk_ch(c, i)
+    // on (K as the A operand, q as B: both from the same thread, so any
+    // per-thread assignment is consistent).  In p.V, row m = g of the A tile
+    // (V^T) in MMA j is channel pv_ch(g, j) and row m = g + 8 is
+    // pv_ch(g, D/16 + j).  Int8 rows (<= 128 B) use contiguous runs; float
+    // rows take 16-byte chunks 2c, 2c+1 (q.k) and chunk g (p.V) of every
+    // panel, which keeps the loads of a quarter warp on distinct banks.
+    static constexpr int CH_ELEMS = 16 / ELEM;  // channels per 16-byte chunk
+    // 16-byte chunk k (0 .. ROW/64 - 1) of thread c's q.k slice, counted over the panels
+    __device__ static __forceinline__ int qk_chunk(int c, int k) {
+        if constexpr (SCALED) return c * (ROW / 64) + k;
+        else return (k >> 1) * 8 + 2 * c + (k & 1);
+    }
+    __device__ static __forceinline__ int qk_ch(int c, int i) {
+        if constexpr (SCALED) return (D / 4) * c + 4 * i;
+        else if constexpr (KV == Kv::BF16) return qk_chunk(c, i >> 1) * CH_ELEMS + 4 * (i & 1);
+        else return qk_chunk(c, i) * CH_ELEMS;
+    }
+    __device__ static __forceinline__ int pv_ch(int g, int l) {  // l: 0 .. D/8 - 1
+        if constexpr (SCALED) return (D / 8) * g + l;
+        else return (l / CH_ELEMS) * (128 / ELEM) + g * CH_ELEMS + l % CH_ELEMS;
+    }
 };
 
 struct StageMeta {
@@ -368,6 +408,7 @@ constexpr uint32_t kFirst = 1u, kLast = 2u, kTerm = 4u;
 
 struct AttnArgs {
     const void* q;
+    uint64_t q_stride;  // elements between q rows
     unsigned char* ws;
     float* partials;
     WsLayout l;
@@ -384,31 +425,24 @@ struct AttnArgs {
     const float* sv;
 };
 
+// Channels [ch, ch + 4) of the staged q row.
 template <typename QT>
-__device__ __forceinline__ void load_q_vals(uint32_t q_smem, int c0, int n, float* out);
-
-// Channels [c0, c0+n) of the staged q row (f32).
+__device__ __forceinline__ void load_q4(uint32_t q_smem, int ch, float* out);
 template <>
-__device__ __forceinline__ void load_q_vals<float>(uint32_t q_smem, int c0, int n, float* out) {
-    for (int i = 0; i < n; i += 4) {
-        uint4 v = lds128(q_smem + (uint32_t)(c0 + i) * 4u);
-        out[i] = __uint_as_float(v.x);
-        out[i + 1] = __uint_as_float(v.y);
-        out[i + 2] = __uint_as_float(v.z);
-        out[i + 3] = __uint_as_float(v.w);
-    }
+__device__ __forceinline__ void load_q4<float>(uint32_t q_smem, int ch, float* out) {
+    const uint4 v = lds128(q_smem + (uint32_t)ch * 4u);
+    out[0] = __uint_as_float(v.x);
+    out[1] = __uint_as_float(v.y);
+    out[2] = __uint_as_float(v.z);
+    out[3] = __uint_as_float(v.w);
 }
 template <>
-__device__ __forceinline__ void load_q_vals<__nv_bfloat16>(uint32_t q_smem, int c0, int n, float* out) {
-    for (int i = 0; i < n; i += 8) {
-        uint4 v = lds128(q_smem + (uint32_t)(c0 + i) * 2u);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            out[i + 2 * k] = bf16_lo_to_f32(w[k]);
-            out[i + 2 * k + 1] = bf16_hi_to_f32(w[k]);
-        }
-    }
+__device__ __forceinline__ void load_q4<__nv_bfloat16>(uint32_t q_smem, int ch, float* out) {
+    const uint2 v = lds64(q_smem + (uint32_t)ch * 2u);
+    out[0] = bf16_lo_to_f32(v.x);
+    out[1] = bf16_hi_to_f32(v.x);
+    out[2] = bf16_lo_to_f32(v.y);
+    out[3] = bf16_hi_to_f32(v.y);
 }
 
 // bf16 term `part` (0: hi, 1: lo, 2: lo2, else 0) of the exact three-term
@@ -421,13 +455,25 @@ __device__ __forceinline__ uint32_t split_term_pack(float a, float b, int part) 
     return part == 0 ? h : part == 1 ? l : part == 2 ? l2 : 0u;
 }
 
-template <int D, typename QT>
-__global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
+// The three bf16x2 terms of an f32 pair: h + l + l2 == (a, b) for normal values.
+__device__ __forceinline__ void split3_pair(float a, float b, uint32_t& h, uint32_t& l, uint32_t& l2) {
+    h = pack_bf16x2(a, b);
+    const uint64_t r = f2_sub(f2_pack(a, b), f2_pack(bf16_lo_to_f32(h), bf16_hi_to_f32(h)));
+    l = pack_bf16x2_f2(r);
+    l2 = pack_bf16x2_f2(f2_sub(r, f2_pack(bf16_lo_to_f32(l), bf16_hi_to_f32(l))));
+}
+
+__device__ __forceinline__ uint32_t u4_word(const uint4& v, int w) {
+    return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+}
+
+template <int D, typename QT, Kv KV>
+__global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                 const __grid_constant__ CUtensorMap map_k_stage, const __grid_constant__ CUtensorMap map_v_stage,
                 const __grid_constant__ CUtensorMap map_ks, const __grid_constant__ CUtensorMap map_vs,
                 const AttnArgs args) {
-    using C = Cfg<D>;
+    using C = Cfg<D, KV>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -457,8 +503,10 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         tma_prefetch_desc(&map_v);
         tma_prefetch_desc(&map_k_stage);
         tma_prefetch_desc(&map_v_stage);
-        tma_prefetch_desc(&map_ks);
-        tma_prefetch_desc(&map_vs);
+        if constexpr (C::SCALED) {
+            tma_prefetch_desc(&map_ks);
+            tma_prefetch_desc(&map_vs);
+        }
     }
     __syncthreads();
     // The kernel before this one on the stream may still be running (programmatic
@@ -532,9 +580,31 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 meta->seg_begin = s_begin;
                 meta->seg_count = s_end - s_begin;
                 meta->n_orphans = n_orphans;
-                const uint32_t bytes = nbox * C::BOX * D * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
+                const uint32_t bytes = nbox * C::BOX * C::ROW * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                if (n == (uint32_t)C::T) {  // full stage: whole-stage boxes for K and V
+                if constexpr (!C::SCALED) {
+                    // float rows: 3-D maps {channel, token, row}, one copy per 128-byte panel
+                    constexpr int PX = 128 / C::ELEM;  // channels per panel
+                    if (n == (uint32_t)C::T) {
+#pragma unroll
+                        for (int p = 0; p < C::PANELS; ++p) {
+                            tma_load_3d(st + C::OFF_K + p * C::T * 128, &map_k_stage, &full[slot], p * PX, (int32_t)t,
+                                        (int32_t)sd.row);
+                            tma_load_3d(st + C::OFF_V + p * C::T * 128, &map_v_stage, &full[slot], p * PX, (int32_t)t,
+                                        (int32_t)sd.row);
+                        }
+                    } else {
+                        for (uint32_t b = 0; b < nbox; ++b) {
+#pragma unroll
+                            for (int p = 0; p < C::PANELS; ++p) {
+                                tma_load_3d(st + C::OFF_K + p * C::T * 128 + b * C::BOX * 128, &map_k, &full[slot],
+                                            p * PX, (int32_t)(t + b * C::BOX), (int32_t)sd.row);
+                                tma_load_3d(st + C::OFF_V + p * C::T * 128 + b * C::BOX * 128, &map_v, &full[slot],
+                                            p * PX, (int32_t)(t + b * C::BOX), (int32_t)sd.row);
+                            }
+                        }
+                    }
+                } else if (n == (uint32_t)C::T) {  // full stage: whole-stage boxes for K and V
 #pragma unroll
                     for (int b = 0; b < C::STAGE_BOXES; ++b) {
                         tma_load_2d(st + C::OFF_K + b * C::STAGE_BOX * D, &map_k_stage, &full[slot], 0,
@@ -549,12 +619,13 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                     }
                 }
 #pragma unroll
-                for (int b = 0; b < C::SC_BOXES; ++b) {
+                for (int b = 0; b < C::SC_BOXES; ++b) {  // int8 only (no boxes for float rows)
                     tma_load_1d(st + C::OFF_KS + b * C::SC_BOX * 4, &map_ks, &full[slot], (int32_t)(ksx + b * C::SC_BOX));
                     tma_load_1d(st + C::OFF_VS + b * C::SC_BOX * 4, &map_vs, &full[slot], (int32_t)(vsx + b * C::SC_BOX));
                 }
                 if (first) {
-                    const unsigned char* qrow = reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * q_bytes;
+                    const unsigned char* qrow =
+                        reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * args.q_stride * sizeof(QT);
                     if (waited) {
                         bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
                     } else {
@@ -626,7 +697,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         const uint32_t seg_begin = m2w.x, n_pre = min(m2w.y, (uint32_t)C::QSLOTS), n_orphans = m2w.z;
         for (uint32_t k = 1 + warp; k < n_pre; k += C::NC) {
             const uint32_t r = segs[seg_begin + k].row;
-            const QT* qr = reinterpret_cast<const QT*>(args.q) + (uint64_t)r * D;
+            const QT* qr = reinterpret_cast<const QT*>(args.q) + (uint64_t)r * args.q_stride;
             __nv_bfloat16* qslot = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_QT + k * C::QT_BYTES);
 #pragma unroll
             for (int e = 0; e < D / 32; ++e) {
@@ -675,24 +746,22 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                     if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
                     return;
                 }
-                const uint32_t qt = smem_addr(smem + C::OFF_QT + seg_count * C::QT_BYTES) + (uint32_t)g * (D * 2) +
-                                    (uint32_t)c * (D / 2);
+                const uint32_t qt = smem_addr(smem + C::OFF_QT + seg_count * C::QT_BYTES) + (uint32_t)g * (D * 2);
 #pragma unroll
-                for (int i = 0; i < C::NI; i += 2) {
-                    const uint4 w = g < 3 ? lds128(qt + i * 8) : make_uint4(0u, 0u, 0u, 0u);
+                for (int i = 0; i < C::NI; i += 2) {  // channels qk_ch(c, i) .. + 8 are contiguous
+                    const uint4 w = g < 3 ? lds128(qt + 2u * (uint32_t)C::qk_ch(c, i)) : make_uint4(0u, 0u, 0u, 0u);
                     qb[i][0] = w.x;
                     qb[i][1] = w.y;
                     qb[i + 1][0] = w.z;
                     qb[i + 1][1] = w.w;
                 }
             } else {
-                constexpr int QN = D / 4;
-                float qv[QN];
-                load_q_vals<QT>(smem_addr(st + C::OFF_Q), QN * c, QN, qv);
 #pragma unroll
                 for (int i = 0; i < C::NI; ++i) {
-                    const float a0 = qv[4 * i] * args.scale_log2, a1 = qv[4 * i + 1] * args.scale_log2;
-                    const float a2 = qv[4 * i + 2] * args.scale_log2, a3 = qv[4 * i + 3] * args.scale_log2;
+                    float qv[4];
+                    load_q4<QT>(smem_addr(st + C::OFF_Q), C::qk_ch(c, i), qv);
+                    const float a0 = qv[0] * args.scale_log2, a1 = qv[1] * args.scale_log2;
+                    const float a2 = qv[2] * args.scale_log2, a3 = qv[3] * args.scale_log2;
                     qb[i][0] = split_term_pack(a0, a1, g);
                     qb[i][1] = split_term_pack(a2, a3, g);
                 }
@@ -710,8 +779,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         auto blocks = [&](auto nblk_tag, auto masked_tag) {
             constexpr int NBLK = decltype(nblk_tag)::value;
             constexpr bool MASKED = decltype(masked_tag)::value;
-            const uint32_t kt = smem_addr(st + C::OFF_K + tok0 * D);
-            const uint32_t vt = smem_addr(st + C::OFF_V + tok0 * D);
+            const uint32_t kt = smem_addr(st + C::OFF_K + tok0 * C::PANEL);
+            const uint32_t vt = smem_addr(st + C::OFF_V + tok0 * C::PANEL);
             const uint32_t ks = smem_addr(st + C::OFF_KS) + (ks_off + tok0) * 4u;
             const uint32_t vs = smem_addr(st + C::OFF_VS) + (vs_off + tok0) * 4u;
             auto scale = [&](uint32_t addr, int e) -> float {  // e: token index from tok0
@@ -722,16 +791,19 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             // ---- scores: q . k for tokens g and g+8 of each block
             float s_g[NBLK], s_g8[NBLK];
             {
-                uint64_t sg2[NBLK], sg82[NBLK];
                 float sacc[NBLK][2][4];
+#pragma unroll
+                for (int b = 0; b < NBLK; ++b)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) sacc[b][h][0] = sacc[b][h][1] = sacc[b][h][2] = sacc[b][h][3] = 0.f;
+                if constexpr (C::SCALED) {
+                uint64_t sg2[NBLK], sg82[NBLK];
                 uint32_t wa[NBLK][C::NI], wb[NBLK][C::NI];
 #pragma unroll
                 for (int b = 0; b < NBLK; ++b) {
                     const float sg = scale(ks, 16 * b + g), sg8 = scale(ks, 16 * b + g + 8);
                     sg2[b] = f2_pack(sg, sg);
                     sg82[b] = f2_pack(sg8, sg8);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) sacc[b][h][0] = sacc[b][h][1] = sacc[b][h][2] = sacc[b][h][3] = 0.f;
                     const uint32_t kb = kt + b * 16 * D;
                     if constexpr (D == 128) {
                         // 128B swizzle: row e, 16B chunk x stored at chunk x ^ (e & 7).
@@ -767,6 +839,48 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                         b23 = f2_mul(b23, sg82[b]);
                         mma_bf16_16816(sacc[b][i & 1], pack_bf16x2_f2(a01), pack_bf16x2_f2(b01),
                                        pack_bf16x2_f2(a23), pack_bf16x2_f2(b23), qb[i][0], qb[i][1]);
+                    }
+                }
+                } else {
+                    // float rows: thread c's 16-byte chunks qk_chunk(c, k) of tokens g and g + 8
+                    constexpr int NCH = C::ROW / 64;
+                    uint4 ka[NBLK][NCH], kc[NBLK][NCH];
+#pragma unroll
+                    for (int b = 0; b < NBLK; ++b) {
+#pragma unroll
+                        for (int k = 0; k < NCH; ++k) {
+                            const int gc = C::qk_chunk(c, k);
+                            const uint32_t pb = kt + (uint32_t)(gc >> 3) * (C::T * 128) + b * 16 * 128;
+                            const uint32_t sw = (uint32_t)(((gc & 7) ^ g) << 4);  // rows g, g + 8: swizzle phase g
+                            ka[b][k] = lds128(pb + g * 128 + sw);
+                            kc[b][k] = lds128(pb + (g + 8) * 128 + sw);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < C::NI; ++i) {
+#pragma unroll
+                        for (int b = 0; b < NBLK; ++b) {
+                            if constexpr (KV == Kv::BF16) {
+                                // channels qk_ch(c, i) .. + 3: words 2(i&1), 2(i&1)+1 of chunk i/2
+                                const uint4& A = ka[b][i >> 1];
+                                const uint4& B = kc[b][i >> 1];
+                                const int w = 2 * (i & 1);
+                                mma_bf16_16816(sacc[b][i & 1], u4_word(A, w), u4_word(B, w), u4_word(A, w + 1),
+                                               u4_word(B, w + 1), qb[i][0], qb[i][1]);
+                            } else {
+                                // f32: chunk i holds channels qk_ch(c, i) .. + 3; three bf16 terms each
+                                const uint4& A = ka[b][i];
+                                const uint4& B = kc[b][i];
+                                uint32_t a0[3], a1[3], a2[3], a3[3];
+                                split3_pair(__uint_as_float(A.x), __uint_as_float(A.y), a0[0], a0[1], a0[2]);
+                                split3_pair(__uint_as_float(B.x), __uint_as_float(B.y), a1[0], a1[1], a1[2]);
+                                split3_pair(__uint_as_float(A.z), __uint_as_float(A.w), a2[0], a2[1], a2[2]);
+                                split3_pair(__uint_as_float(B.z), __uint_as_float(B.w), a3[0], a3[1], a3[2]);
+#pragma unroll
+                                for (int tm = 0; tm < 3; ++tm)
+                                    mma_bf16_16816(sacc[b][i & 1], a0[tm], a1[tm], a2[tm], a3[tm], qb[i][0], qb[i][1]);
+                            }
+                        }
                     }
                 }
 #pragma unroll
@@ -829,6 +943,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
 
                 // ---- p . V: A = V^T (rows = channels, k = tokens 2c, 2c+1, 2c+8, 2c+9)
                 const int e0 = 16 * b + 2 * c, e1 = e0 + 1, e2 = e0 + 8, e3 = e0 + 9;
+                if constexpr (C::SCALED) {
                 const float v0s = scale(vs, e0), v1s = scale(vs, e1), v2s = scale(vs, e2), v3s = scale(vs, e3);
                 const uint64_t s0 = f2_pack(v0s, v0s), s1 = f2_pack(v1s, v1s);
                 const uint64_t s2 = f2_pack(v2s, v2s), s3 = f2_pack(v3s, v3s);
@@ -882,6 +997,51 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                     // accumulator j: channel 8g + j (m = g) and 8g + 4 + j (m = g + 8)
                     pv_mma4(0, v0.x, v1.x, v2.x, v3.x, v0.y, v1.y, v2.y, v3.y);
                 }
+                } else {
+                    // float rows: chunk g of every panel of tokens e0..e3; MMA j takes
+                    // channels pv_ch(g, j) (m = g) and pv_ch(g, D/16 + j) (m = g + 8)
+                    constexpr int NVC = C::PANELS, CE = C::CH_ELEMS;
+                    uint4 vv[4][NVC];
+                    const int er[4] = {e0, e1, e2, e3};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const uint32_t sw = (uint32_t)((g ^ (er[t] & 7)) << 4);
+#pragma unroll
+                        for (int k = 0; k < NVC; ++k) {
+                            vv[t][k] = lds128(vt + (uint32_t)k * (C::T * 128) + (uint32_t)er[t] * 128u + sw);
+                            // past the segment end p is 0, but the row there may hold anything (NaN)
+                            if constexpr (MASKED)
+                                if (er[t] >= nv) vv[t][k] = make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < C::NJ; ++j) {
+                        constexpr int H = D / 16;
+                        if constexpr (KV == Kv::BF16) {
+                            // bf16 pairs of two tokens for one channel: halves (j & 1) of word w
+                            const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
+                            const int p0 = j / CE, w0 = (j % CE) >> 1, p1 = (H + j) / CE, w1 = ((H + j) % CE) >> 1;
+                            mma_bf16_16816(acc[j], __byte_perm(u4_word(vv[0][p0], w0), u4_word(vv[1][p0], w0), sel),
+                                           __byte_perm(u4_word(vv[0][p1], w1), u4_word(vv[1][p1], w1), sel),
+                                           __byte_perm(u4_word(vv[2][p0], w0), u4_word(vv[3][p0], w0), sel),
+                                           __byte_perm(u4_word(vv[2][p1], w1), u4_word(vv[3][p1], w1), sel), pb0, pb1);
+                        } else {
+                            const int p0 = j / CE, f0 = j % CE, p1 = (H + j) / CE, f1 = (H + j) % CE;
+                            uint32_t a0[3], a1[3], a2[3], a3[3];
+                            split3_pair(__uint_as_float(u4_word(vv[0][p0], f0)), __uint_as_float(u4_word(vv[1][p0], f0)),
+                                        a0[0], a0[1], a0[2]);
+                            split3_pair(__uint_as_float(u4_word(vv[0][p1], f1)), __uint_as_float(u4_word(vv[1][p1], f1)),
+                                        a1[0], a1[1], a1[2]);
+                            split3_pair(__uint_as_float(u4_word(vv[2][p0], f0)), __uint_as_float(u4_word(vv[3][p0], f0)),
+                                        a2[0], a2[1], a2[2]);
+                            split3_pair(__uint_as_float(u4_word(vv[2][p1], f1)), __uint_as_float(u4_word(vv[3][p1], f1)),
+                                        a3[0], a3[1], a3[2]);
+#pragma unroll
+                            for (int tm = 0; tm < 3; ++tm)
+                                mma_bf16_16816(acc[j], a0[tm], a1[tm], a2[tm], a3[tm], pb0, pb1);
+                        }
+                    }
+                }
             }
         };
         using I1 = std::integral_constant<int, 1>;
@@ -915,9 +1075,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 a += __shfl_xor_sync(0xffffffffu, a, 2);
                 b += __shfl_xor_sync(0xffffffffu, b, 2);
                 if (c == (j & 3)) {
-                    // accumulator j holds channels (D/8) g + j and (D/8) g + D/16 + j
-                    mine[(D / 8) * g + j] = a;
-                    mine[(D / 8) * g + D / 16 + j] = b;
+                    // accumulator j holds channels pv_ch(g, j) and pv_ch(g, D/16 + j)
+                    mine[C::pv_ch(g, j)] = a;
+                    mine[C::pv_ch(g, D / 16 + j)] = b;
                 }
             }
             float zt = zsum;
@@ -1020,11 +1180,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
                           a.out);
 }
 
-template <int D, typename QT>
+template <int D, typename QT, Kv KV>
 cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
-    using C = Cfg<D>;
+    using C = Cfg<D, KV>;
     AttnArgs args{};
     args.q = L.q;
+    args.q_stride = L.q_stride;
     args.ws = L.ws;
     args.partials = reinterpret_cast<float*>(L.ws + L.layout.partials);
     args.l = L.layout;
@@ -1049,7 +1210,7 @@ cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = L.use_pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT>, L.map_k, L.map_v, L.map_k_stage, L.map_v_stage, L.map_ks,
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT, KV>, L.map_k, L.map_v, L.map_k_stage, L.map_v_stage, L.map_ks,
                               L.map_vs, args);
 }
 
@@ -1079,23 +1240,42 @@ cudaError_t launch_combine_t(const AttnLaunch& L, cudaStream_t stream) {
 
 }  // namespace
 
+namespace {
+template <int D, typename QT, Kv KV>
+cudaError_t configure_one() {
+    return cudaFuncSetAttribute(attn_kernel<D, QT, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Cfg<D, KV>::SMEM_BYTES);
+}
+template <Kv KV>
+cudaError_t configure_kind() {
+    cudaError_t e;
+    if ((e = configure_one<128, float, KV>()) != cudaSuccess) return e;
+    if ((e = configure_one<128, __nv_bfloat16, KV>()) != cudaSuccess) return e;
+    if ((e = configure_one<64, float, KV>()) != cudaSuccess) return e;
+    return configure_one<64, __nv_bfloat16, KV>();
+}
+template <Kv KV>
+cudaError_t launch_kind(const AttnLaunch& L, cudaStream_t stream) {
+    const bool bq = L.q_dtype == PP_DTYPE_BF16;
+    if (L.arena.head_dim == 128)
+        return bq ? launch_attn_t<128, __nv_bfloat16, KV>(L, stream) : launch_attn_t<128, float, KV>(L, stream);
+    return bq ? launch_attn_t<64, __nv_bfloat16, KV>(L, stream) : launch_attn_t<64, float, KV>(L, stream);
+}
+}  // namespace
+
 cudaError_t configure_attention_kernels(int /*device*/) {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(attn_kernel<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Cfg<128>::SMEM_BYTES)) != cudaSuccess)
-        return e;
-    if ((e = cudaFuncSetAttribute(attn_kernel<128, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Cfg<128>::SMEM_BYTES)) != cudaSuccess)
-        return e;
-    if ((e = cudaFuncSetAttribute(attn_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Cfg<64>::SMEM_BYTES)) != cudaSuccess)
-        return e;
-    return cudaFuncSetAttribute(attn_kernel<64, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                Cfg<64>::SMEM_BYTES);
+    if ((e = configure_kind<Kv::I8>()) != cudaSuccess) return e;
+    if ((e = configure_kind<Kv::BF16>()) != cudaSuccess) return e;
+    return configure_kind<Kv::F32>();
 }
 
 uint32_t attention_scale_box_elems() { return Cfg<128>::SC_BOX; }
 uint32_t attention_stage_tokens() { return Cfg<128>::STAGE_BOX; }
+uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind) {
+    if (kv_kind == kKvBf16) return head_dim == 128 ? Cfg<128, Kv::BF16>::T : Cfg<64, Kv::BF16>::T;
+    return head_dim == 128 ? Cfg<128, Kv::F32>::T : Cfg<64, Kv::F32>::T;
+}
 
 cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
     PlanArgs a{};
@@ -1115,9 +1295,9 @@ cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
 }
 
 cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream) {
-    const bool bq = L.q_dtype == PP_DTYPE_BF16;
-    if (L.arena.head_dim == 128) return bq ? launch_attn_t<128, __nv_bfloat16>(L, stream) : launch_attn_t<128, float>(L, stream);
-    return bq ? launch_attn_t<64, __nv_bfloat16>(L, stream) : launch_attn_t<64, float>(L, stream);
+    if (L.kv_kind == kKvBf16) return launch_kind<Kv::BF16>(L, stream);
+    if (L.kv_kind == kKvF32) return launch_kind<Kv::F32>(L, stream);
+    return launch_kind<Kv::I8>(L, stream);
 }
 
 cudaError_t launch_combine(const AttnLaunch& L, cudaStream_t stream) {

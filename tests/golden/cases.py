@@ -210,3 +210,54 @@ def renyi_case(seed: int, batch: int, choices: int, guidance: int) -> dict:
     if batch > 7:
         bounds[7] = (1, 0)                 # empty window
     return dict(raw=raw, uniforms=uniforms, bounds=bounds)
+
+
+# ------------------------------------------------------- float-KV attention
+# Inputs for the reference's float-KV fused decode attention
+# (decode_attention.cu, fused_attention.rs): name, seed, KV dtype, batch,
+# heads, size (the key length), row capacity (row stride in tokens, >= size),
+# lengths ("none" or "ragged"), split_tokens, q row stride (elements).
+# Every token at or past its row's length holds NaN: the kernel must never
+# let it reach the output.  Ragged lengths include 0 and size + 1 (NaN rows),
+# 1 and size.
+FLOAT_CASES = [
+    ("fa_prep", 0, "f32", 1, 1, 257, 257, "none", 128, 64),
+    ("fa_f32_dense", 71, "f32", 3, 2, 300, 300, "none", 0, 64),
+    ("fa_bf16_ragged", 72, "bf16", 4, 3, 1024, 1100, "ragged", 0, 64),
+    ("fa_bf16_split", 73, "bf16", 2, 4, 700, 700, "ragged", 128, 128),
+    ("fa_f32_clamp", 74, "f32", 5, 2, 100, 128, "ragged", 1, 64),
+    ("fa_f32_peaky", 75, "f32", 2, 2, 513, 520, "none", 0, 80),
+    ("fa_bf16_wide", 76, "bf16", 2, 2, 1024, 1024, "none", 5000, 64),
+]
+
+
+def float_case(seed: int, dtype: str, batch: int, heads: int, size: int, cap: int, lengths: str,
+               q_stride: int, d: int = 64) -> dict:
+    """q f32 [rows, q_stride] (first d used); k, v [rows, cap, d] as f32 or
+    bf16 bits (uint16); lengths u32 [batch] or None."""
+    rows = batch * heads
+    if seed == 0:  # the reference's prepare_optional_kernels fixture (mod.rs:447-452): zeros
+        q = np.zeros((rows, q_stride), np.float32)
+        k = np.zeros((rows, cap, d), np.float32)
+        v = np.zeros((rows, cap, d), np.float32)
+        lens = None
+    else:
+        g = np.random.Generator(np.random.PCG64(seed))
+        q = g.standard_normal((rows, q_stride)).astype(np.float32)
+        k = g.standard_normal((rows, cap, d)).astype(np.float32)
+        v = g.standard_normal((rows, cap, d)).astype(np.float32)
+        if seed == 75:  # peaky softmax: large scores, ties of the maximum across splits
+            k *= np.float32(6.0)
+            k[0, 10] = k[0, 400]
+        lens = None
+        if lengths == "ragged":
+            lens = g.integers(1, size + 1, batch).astype(np.uint32)
+            edge = [size, 1, 0, size + 1]
+            lens[:min(batch, 4)] = edge[:min(batch, 4)]
+        for r in range(rows):
+            n = size if lens is None else int(lens[r // heads])
+            k[r, min(n, cap):] = np.nan
+            v[r, min(n, cap):] = np.nan
+    if dtype == "bf16":
+        k, v = to_bf16_bits(k), to_bf16_bits(v)
+    return dict(q=q, k=k, v=v, lengths=lens)
