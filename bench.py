@@ -690,7 +690,7 @@ def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
-                traffic = json.load(f).get("float")
+                traffic = json.load(f).get("float" if kv_t == torch.bfloat16 else "float_f32")
         except Exception:
             traffic = None
     if rank == 0:
