@@ -393,15 +393,16 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     24 layers (RMSNorm, QKV projection, fused q/k RMSNorm + RoPE + int8 append,
     int8 decode attention over history + the new token, output projection,
     RMSNorm, gate/up projection, SwiGLU, down projection) and the final
-    RMSNorm.  Projections are cuBLAS GEMMs; the rest are this library's
-    kernels.  Each step appends at the next slot, so the context grows by one
+    RMSNorm.  Projections are cuBLAS GEMMs (this library's decode-row GEMM
+    with --gemm rows); the rest are this library's kernels.  Each step appends at the next slot, so the context grows by one
     token per step.  Branches are independent: no collective in the step."""
     D = pp.decoder
     cfg = D.DecoderConfig(layers=w["layers"], width=w["width"], heads=w["heads"], head_dim=w["d"],
                           ffn_hidden=w["ffn"], max_context=w["ctx"] + args.warmup + args.steps + 8)
     B, L0 = w["branches"], w["ctx"]
     steps = args.steps
-    model = D.SyntheticDecoder(cfg, branches=B, capacity=cfg.max_context, device=dev, seed=1234 + rank)
+    model = D.SyntheticDecoder(cfg, branches=B, capacity=cfg.max_context, device=dev, seed=1234 + rank,
+                               gemm=args.gemm)
     model.fill_history(None, seed=99 + rank)
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
@@ -496,6 +497,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
             "config": {"workload": "cfg3", "desc": w["desc"], "branches_per_gpu": B, "layers": cfg.layers,
                        "width": cfg.width, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn_hidden": cfg.ffn_hidden,
                        "context": L0, "parameters": cfg.parameters(), "cuda_graph": graph is not None,
+                       "projections": "decode-row GEMM (rows_gemm)" if model.rows_gemm else "cuBLAS",
                        "parallelism": f"branch shards x{world}, weights replicated (no collective in the step)",
                        "l2": "weights 2.5 GB + history 3.3 GB per step, larger than L2; no flush"},
             "tokens_per_s": tokens_per_s,
@@ -505,7 +507,8 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "timed": "whole decode step (weights + int8 history bytes) per step, CUDA events"},
             "clocks": clocks.summary(),
             "e2e": e2e,
-            "gpu_launches": steps * (1 + cfg.layers * 5 + 1),
+            # plan; per layer 2 rmsnorm, qkv_rope_append, attention, swiglu (+ 4 decode-row GEMMs); final rmsnorm
+            "gpu_launches": steps * (1 + cfg.layers * (5 + (4 if model.rows_gemm else 0)) + 1),
             "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
@@ -736,6 +739,8 @@ def main() -> int:
     ap.add_argument("--no-graph", action="store_true", help="cfg3: launch the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-prefetch", action="store_true", help="never stream history before the previous kernel ends")
     ap.add_argument("--kv-dtype", choices=["bf16", "f32"], default=None, help="float workload: K/V element type")
+    ap.add_argument("--gemm", choices=["rows", "cublas"], default="cublas",
+                    help="cfg3: projections by cuBLAS (default) or the decode-row GEMM")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     if args.layers:

@@ -1,4 +1,5 @@
-// On-device self-check run before int8 caches are created.
+// On-device self-checks: the one run before int8 caches are created, and the
+// one that gates the optional fused float-KV decode kernels.
 //
 // Restates the reference's preparation check, app/src/model/int8_kv_ops.rs:57-103:
 // the same closed-form fixtures, the same host loops, the same tolerances and
@@ -6,6 +7,7 @@
 // safe fallback to floating KV).  The device path exercised is the product
 // path: pp_b200_quantize, pp_b200_dequantize and pp_b200_decode_attention.
 #include <cmath>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -216,7 +218,84 @@ int32_t selfcheck() {
     return PP_STATUS_OK;
 }
 
+// prepare_optional_kernels (app/src/model/mod.rs:440-460): zero inputs through
+// the fused float attention (and SwiGLU), every output finite and within 1e-6.
+int32_t optional_selfcheck(uint32_t fusion, uint32_t split_k, int32_t dtype, uint32_t width, uint32_t ffn_hidden) {
+    const size_t elem = dtype == PP_DTYPE_F32 ? 4 : 2;
+    DevBuf dq, dk, dv, dout, dws;
+    PP_TRY_CUDA(dq.alloc(width * 4));
+    PP_TRY_CUDA(dk.alloc(257 * width * elem));
+    PP_TRY_CUDA(dv.alloc(257 * width * elem));
+    PP_TRY_CUDA(dout.alloc(width * 4));
+    PP_TRY_CUDA(cudaMemset(dq.p, 0, width * 4));
+    PP_TRY_CUDA(cudaMemset(dk.p, 0, 257 * width * elem));
+    PP_TRY_CUDA(cudaMemset(dv.p, 0, 257 * width * elem));
+    PpFloatKv kv{};
+    kv.struct_size = sizeof kv;
+    kv.rows = 1;
+    kv.heads = 1;
+    kv.head_dim = width;
+    kv.tokens = 257;
+    kv.dtype = dtype;
+    kv.k_row_stride = kv.v_row_stride = 257ull * width;
+    kv.k = dk.p;
+    kv.v = dv.p;
+    PpAttnParams p{};
+    p.struct_size = sizeof p;
+    p.split_tokens = split_k ? 128u : 0u;
+    p.q_dtype = PP_DTYPE_F32;
+    p.out_dtype = PP_DTYPE_F32;
+    const size_t ws_bytes = pp_b200_float_attention_workspace_size(&kv, &p);
+    PP_TRY_CUDA(dws.alloc(ws_bytes));
+    PP_TRY(pp_b200_decode_attention_float(&kv, &p, dq.p, width, nullptr, dout.p, dws.p, ws_bytes, nullptr, nullptr));
+    PP_TRY_CUDA(cudaDeviceSynchronize());
+    std::vector<float> got(width);
+    PP_TRY_CUDA(cudaMemcpy(got.data(), dout.p, width * 4, cudaMemcpyDeviceToHost));
+    for (float x : got)
+        if (!std::isfinite(x) || std::fabs(x) > 1e-6f)
+            return pp::fail_msg(PP_STATUS_PRECONDITION, "融合注意力准备验证失败");
+    if (fusion) {
+        const uint64_t n = 2ull * ffn_hidden;
+        DevBuf dg, dh;
+        PP_TRY_CUDA(dg.alloc(n * elem));
+        PP_TRY_CUDA(dh.alloc(ffn_hidden * elem));
+        PP_TRY_CUDA(cudaMemset(dg.p, 0, n * elem));
+        PP_TRY(pp_b200_swiglu(dg.p, dh.p, 1, ffn_hidden, dtype, nullptr));
+        PP_TRY_CUDA(cudaDeviceSynchronize());
+        std::vector<float> h(ffn_hidden);
+        if (dtype == PP_DTYPE_F32) {
+            PP_TRY_CUDA(cudaMemcpy(h.data(), dh.p, ffn_hidden * 4, cudaMemcpyDeviceToHost));
+        } else {
+            std::vector<uint16_t> b(ffn_hidden);
+            PP_TRY_CUDA(cudaMemcpy(b.data(), dh.p, ffn_hidden * 2, cudaMemcpyDeviceToHost));
+            for (uint32_t i = 0; i < ffn_hidden; ++i) {
+                const uint32_t u = (uint32_t)b[i] << 16;
+                std::memcpy(&h[i], &u, 4);
+            }
+        }
+        for (float x : h)
+            if (!std::isfinite(x) || std::fabs(x) > 1e-6f) return pp::fail_msg(PP_STATUS_PRECONDITION, "融合FFN准备验证失败");
+    }
+    return PP_STATUS_OK;
+}
+
 }  // namespace
+
+extern "C" int32_t pp_b200_prepare_optional(int32_t device, uint32_t fusion, uint32_t split_k, int32_t model_dtype,
+                                            uint32_t head_width, uint32_t ffn_hidden) {
+    if (!fusion && !split_k) return PP_STATUS_OK;
+    if ((head_width != 64 && head_width != 128) || (model_dtype != PP_DTYPE_F32 && model_dtype != PP_DTYPE_BF16) ||
+        (fusion && ffn_hidden == 0))
+        return pp::fail_msg(PP_STATUS_PRECONDITION, "当前模型后端不支持此融合解码路径");
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return pp::fail_msg(PP_STATUS_PRECONDITION, "当前模型后端不支持此融合解码路径");
+    if ((e = cudaSetDevice(device)) != cudaSuccess)
+        return pp::fail_msg(PP_STATUS_PRECONDITION, "当前模型后端不支持此融合解码路径");
+    const int32_t s = optional_selfcheck(fusion, split_k, model_dtype, head_width, ffn_hidden);
+    cudaSetDevice(prev);
+    return s;
+}
 
 extern "C" int32_t pp_b200_prepare(int32_t device) {
     int prev = 0;

@@ -190,6 +190,9 @@ __global__ void __launch_bounds__(32 * kQkvWarps) qkv_rope_kernel(const QkvArgs 
 // reference's rounding of exp, the sum and the quotient (graph_ops.cu:60-74).
 template <bool BF>
 __global__ void __launch_bounds__(256) swiglu_kernel(const void* in, void* out, uint64_t rows, uint32_t hidden) {
+    // a dependent decode-row GEMM may start streaming its weights now; it
+    // waits for this kernel before reading the activations
+    pdl_launch_dependents();
     const uint64_t n = rows * hidden, stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         const uint64_t row = i / hidden, c = i % hidden;
@@ -209,6 +212,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const void* in, void* out, 
 template <bool BF>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* x, const void* residual, void* x_sum,
                                                       const void* weight, void* out, uint32_t width, float eps) {
+    pdl_launch_dependents();  // as swiglu_kernel
     __shared__ float part[8];
     const uint64_t base = (uint64_t)blockIdx.x * width;
     float ss = 0.f;
@@ -277,6 +281,7 @@ __device__ __forceinline__ void store8(void* p, uint64_t i, const float (&v)[8])
 template <bool BF>
 __global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const void* x, const void* residual, void* x_sum,
                                                            const void* weight, void* out, uint32_t width, float eps) {
+    pdl_launch_dependents();  // as swiglu_kernel
     __shared__ float part[32];
     const uint64_t i = (uint64_t)blockIdx.x * width + threadIdx.x * 8u;
     float v[8];

@@ -112,33 +112,80 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
 
 // The same over 16-byte groups of codes (16 elements of one row, d % 16 == 0):
 // one 16-byte load of codes, one scale, 16 products, 32 or 64 bytes stored.
+// Each thread keeps kDqUnroll groups in flight (loads issued before any use)
+// and the grid is one resident wave, so the loads of a whole SM cover the
+// memory latency.  The codes become floats exactly (byte permute into
+// 2^23 + 128 + c, packed subtract of the bias), the product is the reference's
+// f32 multiply and the bf16 pack rounds to nearest even.
+constexpr int kDqUnroll = 4;
+
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream(uint4* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 template <typename O>
-__global__ void __launch_bounds__(256) dequantize16_kernel(const uint4* __restrict__ packed,
+__device__ __forceinline__ void dequant_group(uint4 w, float s, int round_bf16, O* out) {
+    const uint64_t s2 = f2_pack(s, s);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    uint64_t p[8];  // element pairs (2k, 2k+1)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        i8x4_to_f32x2(words[k], p[2 * k], p[2 * k + 1]);
+        p[2 * k] = f2_mul(p[2 * k], s2);
+        p[2 * k + 1] = f2_mul(p[2 * k + 1], s2);
+    }
+    if constexpr (std::is_same<O, float>::value) {
+        uint4* o = reinterpret_cast<uint4*>(out);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float a, b, c, d;
+            f2_unpack(p[2 * k], a, b);
+            f2_unpack(p[2 * k + 1], c, d);
+            if (round_bf16) {
+                a = bf16_round(a);
+                b = bf16_round(b);
+                c = bf16_round(c);
+                d = bf16_round(d);
+            }
+            st_stream(o + k, make_uint4(__float_as_uint(a), __float_as_uint(b), __float_as_uint(c), __float_as_uint(d)));
+        }
+    } else {
+        uint4* o = reinterpret_cast<uint4*>(out);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            st_stream(o + k, make_uint4(pack_bf16x2_f2(p[4 * k]), pack_bf16x2_f2(p[4 * k + 1]),
+                                        pack_bf16x2_f2(p[4 * k + 2]), pack_bf16x2_f2(p[4 * k + 3])));
+    }
+}
+
+template <typename O>
+__global__ void __launch_bounds__(256, 4) dequantize16_kernel(const uint4* __restrict__ packed,
                                                            const float* __restrict__ scales, uint64_t groups,
                                                            uint32_t groups_per_row, int round_bf16, O* __restrict__ out) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < groups; i += stride) {
-        const uint4 w = packed[i];
-        const float s = __ldg(scales + i / groups_per_row);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-        float v[16];
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + (kDqUnroll - 1) * stride < groups; i += kDqUnroll * stride) {
+        uint4 w[kDqUnroll];
+        float s[kDqUnroll];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            v[k] = (float)(int8_t)(words[k / 4] >> (8 * (k % 4))) * s;
-            if (round_bf16) v[k] = bf16_round(v[k]);
+        for (int u = 0; u < kDqUnroll; ++u) {
+            w[u] = ld_stream(packed + i + u * stride);
+            s[u] = __ldg(scales + (i + u * stride) / groups_per_row);
         }
-        if constexpr (std::is_same<O, float>::value) {
-            float4* o = reinterpret_cast<float4*>(out + i * 16);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) o[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-        } else {
-            uint4* o = reinterpret_cast<uint4*>(out + i * 16);
-#pragma unroll
-            for (int k = 0; k < 2; ++k)
-                o[k] = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
-                                  pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
-        }
+        for (int u = 0; u < kDqUnroll; ++u) dequant_group<O>(w[u], s[u], round_bf16, out + (i + u * stride) * 16);
     }
+    for (; i < groups; i += stride)
+        dequant_group<O>(ld_stream(packed + i), __ldg(scales + i / groups_per_row), round_bf16, out + i * 16);
 }
 
 // Row-prefix copy between arenas: block (row, chunk) copies 16-byte vectors of
@@ -225,7 +272,9 @@ cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, uint64
     if (vec) {
         const uint64_t groups = n / 16;
         const uint64_t blocks = (groups + 255) / 256;
-        const uint32_t grid = (uint32_t)(blocks < 148u * 16u ? blocks : 148u * 16u);
+        // one resident wave: 4 blocks of 256 threads per SM (<= 64 registers a
+        // thread), 4 x 16 bytes in flight per thread = 64 KB per SM
+        const uint32_t grid = (uint32_t)(blocks < 148u * 4u ? blocks : 148u * 4u);
         if (out_dtype == PP_DTYPE_F32)
             dequantize16_kernel<float><<<grid, 256, 0, stream>>>(reinterpret_cast<const uint4*>(packed), scales, groups,
                                                                  d / 16, round_bf16, (float*)out);

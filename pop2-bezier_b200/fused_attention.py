@@ -102,3 +102,14 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lengths:
                                                  ops._ptr(lengths), ops._ptr(out), ops._ptr(workspace),
                                                  workspace.numel(), ops._ptr(status), ops._stream(q)))
     return out
+
+
+def prepare_optional_kernels(device: torch.device | int, fusion: bool, split_k: bool, *,
+                             dtype: torch.dtype = torch.bfloat16, head_width: int = 64, ffn_hidden: int = 0) -> None:
+    """PrimitiveModel::prepare_optional_kernels (mod.rs:440-460): on-device
+    zero-input checks of the fused attention (and SwiGLU with `fusion`);
+    raises PreconditionError with the reference's messages."""
+    idx = device.index if isinstance(device, torch.device) else int(device)
+    code = N.DTYPE_F32 if dtype == torch.float32 else N.DTYPE_BF16
+    N.check(N.lib.pp_b200_prepare_optional(0 if idx is None else idx, int(fusion), int(split_k), code, head_width,
+                                           ffn_hidden))

@@ -240,3 +240,20 @@ def test_full_size_properties(pp, oracle, cuda):
     vb = v[sample].view(torch.int16).cpu().numpy().view(np.uint16)
     want = oracle.float_attention(q[sample, 0].cpu().numpy(), kb, vb, None, 1, threads=oracle.max_threads())
     np.testing.assert_allclose(out[sample], want, **TIGHT)
+
+
+def test_prepare_optional_rejects_unsupported_widths(pp):
+    """mod.rs:444-446: the fused path needs a supported head width."""
+    N = pp._native
+    assert N.lib.pp_b200_prepare_optional(0, 0, 0, N.DTYPE_BF16, 96, 0) == N.STATUS_OK  # nothing requested
+    assert N.lib.pp_b200_prepare_optional(0, 0, 1, N.DTYPE_BF16, 96, 0) == N.STATUS_PRECONDITION
+    assert N.last_error() == "当前模型后端不支持此融合解码路径"
+    assert N.lib.pp_b200_prepare_optional(0, 1, 0, N.DTYPE_BF16, 64, 0) == N.STATUS_PRECONDITION
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("fusion,split_k", [(True, True), (False, True), (True, False)])
+def test_prepare_optional_kernels_pass(pp, cuda, dtype, fusion, split_k):
+    pp.fused_attention.prepare_optional_kernels(cuda, fusion, split_k, dtype=dtype, head_width=64, ffn_hidden=5632)
+    pp.fused_attention.prepare_optional_kernels(cuda, fusion, split_k, dtype=dtype, head_width=128, ffn_hidden=300)
