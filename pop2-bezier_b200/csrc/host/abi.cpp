@@ -389,8 +389,10 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     L.out = out;
     L.status = status;
     const uint32_t stage = pp::attention_stage_tokens();  // rows of one whole-stage box
-    if ((s = encode_codes_map(&L.map_k, arena->k, *arena, 16))) return s;
-    if ((s = encode_codes_map(&L.map_v, arena->v, *arena, 16))) return s;
+    for (int i = 0; i < 4; ++i) {
+        if ((s = encode_codes_map(&L.tails.k[i], arena->k, *arena, 16u << i))) return s;
+        if ((s = encode_codes_map(&L.tails.v[i], arena->v, *arena, 16u << i))) return s;
+    }
     if ((s = encode_codes_map(&L.map_k_stage, arena->k, *arena, stage))) return s;
     if ((s = encode_codes_map(&L.map_v_stage, arena->v, *arena, stage))) return s;
     if ((s = encode_scale_map(&L.map_ks, &L.ks_mis, arena->k_scale, *arena))) return s;
@@ -448,8 +450,10 @@ int32_t pp_b200_decode_attention_float(const PpFloatKv* kv, const PpAttnParams* 
     L.out = out;
     L.status = status;
     const uint32_t stage = pp::attention_float_stage_tokens(kv->head_dim, L.kv_kind);
-    if ((s = encode_float_map(&L.map_k, kv->k, kv->k_row_stride, *kv, 16))) return s;
-    if ((s = encode_float_map(&L.map_v, kv->v, kv->v_row_stride, *kv, 16))) return s;
+    for (int i = 0; i < 4; ++i) {
+        if ((s = encode_float_map(&L.tails.k[i], kv->k, kv->k_row_stride, *kv, 16u << i))) return s;
+        if ((s = encode_float_map(&L.tails.v[i], kv->v, kv->v_row_stride, *kv, 16u << i))) return s;
+    }
     if ((s = encode_float_map(&L.map_k_stage, kv->k, kv->k_row_stride, *kv, stage))) return s;
     if ((s = encode_float_map(&L.map_v_stage, kv->v, kv->v_row_stride, *kv, stage))) return s;
     cudaStream_t st = (cudaStream_t)stream;

@@ -88,6 +88,12 @@ inline WsLayout ws_layout(uint32_t rows, uint32_t capacity, uint32_t head_dim, u
 // Element type of the attended K/V (internal codes, not PP_DTYPE_*).
 constexpr int kKvInt8 = 0, kKvBf16 = 1, kKvF32 = 2;
 
+// Tensor maps for segment tails: the same K / V boxes of 16, 32, 64 and 128
+// tokens, so that a tail of n tokens takes at most 4 copies per tensor.
+struct TailMaps {
+    CUtensorMap k[4], v[4];
+};
+
 struct AttnLaunch {
     // int8 arena geometry; for float K/V, capacity is the key length (size)
     // and k/v/k_scale/v_scale are unused
@@ -110,10 +116,11 @@ struct AttnLaunch {
     bool plan_ready;
     bool prefetch;  // PP_ATTN_PREFETCH_HISTORY
     bool use_pdl;
-    // Tensor maps (host-encoded): K, V codes in 16-token boxes and in
-    // whole-stage boxes, and K, V scales (int8 only).  Float K/V maps are
-    // 3-D {channel, token, row} with one 128-byte panel per box.
-    CUtensorMap map_k, map_v, map_k_stage, map_v_stage, map_ks, map_vs;
+    // Tensor maps (host-encoded): K, V codes in whole-stage boxes and in the
+    // tail boxes, and K, V scales (int8 only).  Float K/V maps are 3-D
+    // {channel, token, row} with one 128-byte panel per box.
+    TailMaps tails;
+    CUtensorMap map_k_stage, map_v_stage, map_ks, map_vs;
     uint32_t ks_mis, vs_mis;  // element offset of the scale arrays inside their maps
 };
 

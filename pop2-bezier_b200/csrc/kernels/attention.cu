@@ -334,7 +334,10 @@ struct Cfg {
     static constexpr int TPW = BOX * NB;            // tokens per consumer warp per stage
     static constexpr int T = TPW * NC;              // tokens per stage
     static constexpr int KV_BYTES = T * ROW;
-    static constexpr int SC_BOX = 160;              // scale elements per TMA box (640 B: keeps every box 128B-aligned)
+    // scale elements per TMA box: one box covers a stage's T tokens plus the
+    // alignment slack (a copy costs the SM's copy engine a fixed ~130 ns on
+    // top of its bytes, so a stage is as few copies as possible)
+    static constexpr int SC_BOX = 256;
     static constexpr int SC_BOXES = SCALED ? (T + 4 + SC_BOX - 1) / SC_BOX : 0;  // T tokens + alignment slack
     static constexpr int SC_BYTES = SC_BOXES * SC_BOX * 4;
     static constexpr int Q_BYTES = D * 4;
@@ -367,10 +370,12 @@ struct Cfg {
     // Tensor-copy destinations in shared memory must be 128-byte aligned, and
     // the swizzled tiles 1024-byte aligned (stage bases are 1024-aligned).
     static_assert((SC_BOX * 4) % 128 == 0 && OFF_KS % 128 == 0 && OFF_VS % 128 == 0, "scale boxes 128B-aligned");
+    static_assert(!SCALED || SC_BOXES == 1, "one scale box per tensor per stage");
     static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && (BOX * PANEL) % 1024 == 0 &&
                       (STAGE_BOX * PANEL) % 1024 == 0 && (T * PANEL) % 1024 == 0,
                   "tiles 1024B-aligned");
     static_assert(STAGE_BYTES % 1024 == 0 && OFF_Q % 16 == 0 && OFF_META % 16 == 0, "stage layout alignment");
+    static_assert(T / BOX < 16, "a tail of fewer than T tokens is at most 15 units: one box each of 128/64/32/16");
     static constexpr int NI = D / 16;  // q.k MMAs per 16-token block (k = 16 channels each)
     static constexpr int NJ = D / 16;  // p.V MMAs per 16-token block (m = 16 channels each)
 
@@ -469,7 +474,7 @@ __device__ __forceinline__ uint32_t u4_word(const uint4& v, int w) {
 
 template <int D, typename QT, Kv KV>
 __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
-    attn_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+    attn_kernel(const __grid_constant__ TailMaps tails,
                 const __grid_constant__ CUtensorMap map_k_stage, const __grid_constant__ CUtensorMap map_v_stage,
                 const __grid_constant__ CUtensorMap map_ks, const __grid_constant__ CUtensorMap map_vs,
                 const AttnArgs args) {
@@ -499,8 +504,10 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
         fence_mbar_init();
     }
     if (warp == C::NC && lane == 0) {
-        tma_prefetch_desc(&map_k);
-        tma_prefetch_desc(&map_v);
+        for (int i = 0; i < 4; ++i) {
+            tma_prefetch_desc(&tails.k[i]);
+            tma_prefetch_desc(&tails.v[i]);
+        }
         tma_prefetch_desc(&map_k_stage);
         tma_prefetch_desc(&map_v_stage);
         if constexpr (C::SCALED) {
@@ -593,15 +600,19 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                             tma_load_3d(st + C::OFF_V + p * C::T * 128, &map_v_stage, &full[slot], p * PX, (int32_t)t,
                                         (int32_t)sd.row);
                         }
-                    } else {
-                        for (uint32_t b = 0; b < nbox; ++b) {
+                    } else {  // segment tail: nbox 16-token units as boxes of 128 / 64 / 32 / 16 tokens
+                        uint32_t off = 0;
+#pragma unroll
+                        for (int i = 3; i >= 0; --i) {
+                            if (!(nbox & (1u << i))) continue;
 #pragma unroll
                             for (int p = 0; p < C::PANELS; ++p) {
-                                tma_load_3d(st + C::OFF_K + p * C::T * 128 + b * C::BOX * 128, &map_k, &full[slot],
-                                            p * PX, (int32_t)(t + b * C::BOX), (int32_t)sd.row);
-                                tma_load_3d(st + C::OFF_V + p * C::T * 128 + b * C::BOX * 128, &map_v, &full[slot],
-                                            p * PX, (int32_t)(t + b * C::BOX), (int32_t)sd.row);
+                                tma_load_3d(st + C::OFF_K + p * C::T * 128 + off * 128, &tails.k[i], &full[slot], p * PX,
+                                            (int32_t)(t + off), (int32_t)sd.row);
+                                tma_load_3d(st + C::OFF_V + p * C::T * 128 + off * 128, &tails.v[i], &full[slot], p * PX,
+                                            (int32_t)(t + off), (int32_t)sd.row);
                             }
+                            off += 16u << i;
                         }
                     }
                 } else if (n == (uint32_t)C::T) {  // full stage: whole-stage boxes for K and V
@@ -612,10 +623,14 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                         tma_load_2d(st + C::OFF_V + b * C::STAGE_BOX * D, &map_v_stage, &full[slot], 0,
                                     (int32_t)(tok + b * C::STAGE_BOX));
                     }
-                } else {  // segment tail: 16-token boxes, none wholly past the segment
-                    for (uint32_t b = 0; b < nbox; ++b) {
-                        tma_load_2d(st + C::OFF_K + b * C::BOX * D, &map_k, &full[slot], 0, (int32_t)(tok + b * C::BOX));
-                        tma_load_2d(st + C::OFF_V + b * C::BOX * D, &map_v, &full[slot], 0, (int32_t)(tok + b * C::BOX));
+                } else {  // segment tail: nbox 16-token units as boxes of 128 / 64 / 32 / 16 tokens
+                    uint32_t off = 0;
+#pragma unroll
+                    for (int i = 3; i >= 0; --i) {
+                        if (!(nbox & (1u << i))) continue;
+                        tma_load_2d(st + C::OFF_K + off * D, &tails.k[i], &full[slot], 0, (int32_t)(tok + off));
+                        tma_load_2d(st + C::OFF_V + off * D, &tails.v[i], &full[slot], 0, (int32_t)(tok + off));
+                        off += 16u << i;
                     }
                 }
 #pragma unroll
@@ -1210,7 +1225,7 @@ cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = L.use_pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT, KV>, L.map_k, L.map_v, L.map_k_stage, L.map_v_stage, L.map_ks,
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT, KV>, L.tails, L.map_k_stage, L.map_v_stage, L.map_ks,
                               L.map_vs, args);
 }
 
