@@ -243,6 +243,13 @@ int32_t pp_b200_decode_attention_float(const PpFloatKv* kv, const PpAttnParams* 
                                        uint64_t q_row_stride, const uint32_t* lengths, void* out, void* workspace,
                                        size_t workspace_bytes, uint32_t* status, void* stream);
 
+/* Diagnostic: runs one bounded wait on a barrier that nothing completes, with
+ * the library's wait loop and a limit of limit_us microseconds (1..10^6), so a
+ * host can confirm on its device that a stalled pipeline ends with
+ * PP_DEV_WAIT_TIMEOUT OR-ed into *status (device memory) and a usable context
+ * instead of a hang.  No counterpart in the reference. */
+int32_t pp_b200_diag_bounded_wait(uint32_t* status, uint32_t limit_us, void* stream);
+
 /* Decodes device status bits into a message (static storage). */
 const char* pp_b200_status_message(uint32_t status_bits);
 

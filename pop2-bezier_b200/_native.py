@@ -42,6 +42,7 @@ EXPORTED = (
     "pp_b200_decode_attention",
     "pp_b200_decode_attention_static",
     "pp_b200_status_message",
+    "pp_b200_diag_bounded_wait",
     "pp_b200_checked_batch_rows",
     "pp_b200_check_write_offsets",
     "pp_b200_sched_partition",
@@ -147,6 +148,7 @@ def _load() -> C.CDLL:
         "pp_b200_decode_attention": (i32, [P(PpKvArena), P(PpAttnParams), vp, vp, vp, vp, vp, vp, sz, vp, vp]),
         "pp_b200_decode_attention_static": (i32, [P(PpKvArena), P(PpAttnParams), vp, vp, vp, vp, vp, vp, vp]),
         "pp_b200_status_message": (C.c_char_p, [u32]),
+        "pp_b200_diag_bounded_wait": (i32, [vp, u32, vp]),
         "pp_b200_checked_batch_rows": (i32, [u64, u32, P(u64)]),
         "pp_b200_check_write_offsets": (i32, [P(u64), u64, u32, u32, u32]),
         "pp_b200_sched_partition": (i32, [P(u64), u32, u32, P(u32), P(u64)]),

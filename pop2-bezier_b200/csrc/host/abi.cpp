@@ -644,4 +644,14 @@ int32_t pp_b200_rows_gemm(const void* x, uint64_t ldx, const void* packed_w, voi
     return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "rows_gemm launch");
 }
 
+int32_t pp_b200_diag_bounded_wait(uint32_t* status, uint32_t limit_us, void* stream) {
+    if (!status || limit_us == 0 || limit_us > 1000000)
+        return fail(PP_STATUS_PRECONDITION, "diag_bounded_wait: status pointer and a limit of 1..1000000 us required");
+    DeviceInfo d;
+    int32_t s;
+    if ((s = device_info(d))) return s;
+    cudaError_t e = pp::launch_wait_probe(status, (uint64_t)limit_us * 1000ull, (cudaStream_t)stream);
+    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "diag_bounded_wait launch");
+}
+
 }  // extern "C"

@@ -162,6 +162,7 @@ cudaError_t configure_attention_kernels(int device);
 uint32_t attention_scale_box_elems();
 uint32_t attention_stage_tokens();
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind);
+cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t stream);
 
 // Decode-row GEMM (gemm.cu): out[m, n] = sum_k x[m, k] w[n, k], m <= 16, bf16.
 bool rows_gemm_supported(uint32_t k);

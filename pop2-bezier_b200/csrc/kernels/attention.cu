@@ -1253,7 +1253,27 @@ cudaError_t launch_combine_t(const AttnLaunch& L, cudaStream_t stream) {
     return cudaLaunchKernelEx(&cfg, combine_kernel<D, QT, OT>, a);
 }
 
+// One bounded wait on an mbarrier that nothing completes: the wait gives up
+// after limit_ns and the kernel reports PP_DEV_WAIT_TIMEOUT, as every wait in
+// this library does, instead of hanging.
+__global__ void wait_probe_kernel(uint32_t* status, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    volatile int never = 0;
+    if (!mbar_wait_bounded(&bar, 0u, &never, limit_ns)) atomicOr(status, PP_DEV_WAIT_TIMEOUT);
+}
+
 }  // namespace
+
+cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t stream) {
+    wait_probe_kernel<<<1, 32, 0, stream>>>(status, limit_ns);
+    return cudaGetLastError();
+}
 
 namespace {
 template <int D, typename QT, Kv KV>

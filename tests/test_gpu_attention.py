@@ -7,6 +7,7 @@ at the BASELINE shapes against the oracle within 2e-3 relative / 1e-3
 absolute, plus size-independent properties at full size."""
 from __future__ import annotations
 
+import ctypes as C
 import os
 
 import numpy as np
@@ -312,3 +313,19 @@ def test_cfg4_long_context_split_sweep(pp, oracle, cuda):
     ref = _oracle_rows(oracle, q, k, v, ks, vs, lens.cpu().numpy(), heads, pick)
     np.testing.assert_allclose(outs[32][pick], ref, rtol=2e-3, atol=1e-3)
     np.testing.assert_allclose(outs[32][pick], ref, rtol=1e-4, atol=5e-5)
+
+
+def test_a_stalled_wait_ends_with_a_status_not_a_hang(pp, oracle, cuda):
+    """Failure detection without a fault: a bounded wait on a barrier that
+    nothing completes gives up after its limit (2 ms here), the status word
+    reports PP_DEV_WAIT_TIMEOUT, and the context keeps working."""
+    N = pp._native
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    N.check(N.lib.pp_b200_diag_bounded_wait(C.c_void_p(status.data_ptr()), 2000,
+                                            C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert int(status.item()) & N.DEV_WAIT_TIMEOUT
+    assert "timed out" in N.status_message(int(status.item()))
+    c = K.prep1()
+    codes, scales = pp.int8_kv_ops.quantize(to_dev(c["x"], cuda))
+    assert torch.isfinite(codes.float()).all()
