@@ -15,6 +15,25 @@
 namespace pp {
 namespace {
 
+// Launches as a programmatic dependent of the previous kernel on the stream:
+// the grid may be scheduled before that kernel ends and waits for it
+// (griddepcontrol.wait) before touching memory, which hides the launch gap.
+template <typename... P, typename... A>
+cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, cudaStream_t stream, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+
 // Element access in the model dtype: bf16 (BF = true) or f32.
 template <bool BF>
 __device__ __forceinline__ float rd(const void* p, uint64_t i) {
@@ -75,8 +94,11 @@ template <int D, bool BF, bool APPEND>
 __global__ void __launch_bounds__(32 * kQkvWarps) qkv_rope_kernel(const QkvArgs a) {
     constexpr int E = D / 32;
     __shared__ float sq[kQkvWarps][D], skk[kQkvWarps][D], svv[kQkvWarps][D];
-    // a dependent attention launch may start now and stream history (which this
-    // kernel does not write); it waits for this kernel before reading q/k/v
+    // launched as a programmatic dependent: wait for the kernel before (the QKV
+    // projection), then let a dependent attention launch start and stream
+    // history (which this kernel does not write); it waits for this kernel
+    // before reading q/k/v
+    pdl_wait_primary();
     pdl_launch_dependents();
     const int t = threadIdx.x & 31, w = threadIdx.x >> 5;
     const uint32_t headrow = blockIdx.x * kQkvWarps + w;
@@ -190,8 +212,10 @@ __global__ void __launch_bounds__(32 * kQkvWarps) qkv_rope_kernel(const QkvArgs 
 // reference's rounding of exp, the sum and the quotient (graph_ops.cu:60-74).
 template <bool BF>
 __global__ void __launch_bounds__(256) swiglu_kernel(const void* in, void* out, uint64_t rows, uint32_t hidden) {
-    // a dependent decode-row GEMM may start streaming its weights now; it
-    // waits for this kernel before reading the activations
+    // launched as a programmatic dependent: wait for the kernel before, then a
+    // dependent decode-row GEMM may start streaming its weights; it waits for
+    // this kernel before reading the activations
+    pdl_wait_primary();
     pdl_launch_dependents();
     const uint64_t n = rows * hidden, stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -212,7 +236,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const void* in, void* out, 
 template <bool BF>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* x, const void* residual, void* x_sum,
                                                       const void* weight, void* out, uint32_t width, float eps) {
-    pdl_launch_dependents();  // as swiglu_kernel
+    pdl_wait_primary();  // as swiglu_kernel
+    pdl_launch_dependents();
     __shared__ float part[8];
     const uint64_t base = (uint64_t)blockIdx.x * width;
     float ss = 0.f;
@@ -281,7 +306,8 @@ __device__ __forceinline__ void store8(void* p, uint64_t i, const float (&v)[8])
 template <bool BF>
 __global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const void* x, const void* residual, void* x_sum,
                                                            const void* weight, void* out, uint32_t width, float eps) {
-    pdl_launch_dependents();  // as swiglu_kernel
+    pdl_wait_primary();  // as swiglu_kernel
+    pdl_launch_dependents();
     __shared__ float part[32];
     const uint64_t i = (uint64_t)blockIdx.x * width + threadIdx.x * 8u;
     float v[8];
@@ -315,8 +341,7 @@ template <int D, bool BF, bool APPEND>
 cudaError_t launch_qkv_t(const QkvArgs& a, cudaStream_t stream) {
     const uint64_t items = (uint64_t)a.rows * a.heads;
     const uint32_t blocks = (uint32_t)((items + kQkvWarps - 1) / kQkvWarps);
-    qkv_rope_kernel<D, BF, APPEND><<<blocks, 32 * kQkvWarps, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(qkv_rope_kernel<D, BF, APPEND>, dim3(blocks), dim3(32 * kQkvWarps), stream, a);
 }
 
 template <bool APPEND>
@@ -357,9 +382,8 @@ cudaError_t launch_qkv_rope(const QkvRopeLaunch& L, cudaStream_t stream) {
 cudaError_t launch_swiglu(const void* in, void* out, uint64_t rows, uint32_t hidden, bool bf, cudaStream_t stream) {
     const uint64_t n = rows * hidden;
     const uint32_t blocks = (uint32_t)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
-    if (bf) swiglu_kernel<true><<<blocks, 256, 0, stream>>>(in, out, rows, hidden);
-    else swiglu_kernel<false><<<blocks, 256, 0, stream>>>(in, out, rows, hidden);
-    return cudaGetLastError();
+    if (bf) return launch_pdl(swiglu_kernel<true>, dim3(blocks), dim3(256), stream, in, out, rows, hidden);
+    return launch_pdl(swiglu_kernel<false>, dim3(blocks), dim3(256), stream, in, out, rows, hidden);
 }
 
 cudaError_t launch_rmsnorm(const void* x, const void* residual, void* x_sum, const void* weight, void* out,
@@ -368,14 +392,18 @@ cudaError_t launch_rmsnorm(const void* x, const void* residual, void* x_sum, con
     if (width % 256 == 0 && width <= 8192 && a16(x) && a16(weight) && a16(out) && (!residual || a16(residual)) &&
         (!x_sum || a16(x_sum))) {
         const uint32_t threads = width / 8;
-        if (bf) rmsnorm_vec_kernel<true><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
-        else rmsnorm_vec_kernel<false><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
-        return cudaGetLastError();
+        if (bf)
+            return launch_pdl(rmsnorm_vec_kernel<true>, dim3((uint32_t)rows), dim3(threads), stream, x, residual, x_sum,
+                              weight, out, width, eps);
+        return launch_pdl(rmsnorm_vec_kernel<false>, dim3((uint32_t)rows), dim3(threads), stream, x, residual, x_sum,
+                          weight, out, width, eps);
     }
     const uint32_t threads = width >= 256 ? 256 : 32 * ((width + 31) / 32);
-    if (bf) rmsnorm_kernel<true><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
-    else rmsnorm_kernel<false><<<(uint32_t)rows, threads, 0, stream>>>(x, residual, x_sum, weight, out, width, eps);
-    return cudaGetLastError();
+    if (bf)
+        return launch_pdl(rmsnorm_kernel<true>, dim3((uint32_t)rows), dim3(threads), stream, x, residual, x_sum, weight,
+                          out, width, eps);
+    return launch_pdl(rmsnorm_kernel<false>, dim3((uint32_t)rows), dim3(threads), stream, x, residual, x_sum, weight,
+                      out, width, eps);
 }
 
 }  // namespace pp
