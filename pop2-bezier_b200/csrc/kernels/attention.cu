@@ -73,6 +73,10 @@ struct PlanArgs {
 };
 
 __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
+    // launched as a programmatic dependent: the lengths may come from the kernel
+    // before.  Dependents are released only when the plan is complete (no early
+    // trigger), so nothing can read a half-written plan.
+    pdl_wait_primary();
     __shared__ uint32_t warp_tot[32];
     __shared__ uint32_t s_n_ctas, s_per_cta, s_total, s_bad;
     PlanHeader* hdr = reinterpret_cast<PlanHeader*>(a.ws);
@@ -1325,8 +1329,7 @@ cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
     a.max_ctas = L.max_ctas;
     a.min_tokens = 32;
     a.status = L.status;
-    plan_kernel<<<1, 1024, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(plan_kernel, dim3(1), dim3(1024), stream, a);
 }
 
 cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream) {

@@ -15,23 +15,6 @@
 namespace pp {
 namespace {
 
-// Launches as a programmatic dependent of the previous kernel on the stream:
-// the grid may be scheduled before that kernel ends and waits for it
-// (griddepcontrol.wait) before touching memory, which hides the launch gap.
-template <typename... P, typename... A>
-cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, cudaStream_t stream, A... args) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
 
 
 // Element access in the model dtype: bf16 (BF = true) or f32.

@@ -58,6 +58,10 @@ __global__ void __launch_bounds__(256) quant_append_kernel(const T* __restrict__
                                                            const uint32_t* __restrict__ offsets, uint32_t commit,
                                                            uint8_t* k_arena, uint8_t* v_arena, float* ks_arena,
                                                            float* vs_arena, uint32_t* status) {
+    // launched as a programmatic dependent: wait for the kernel before.  No early
+    // trigger: the history this kernel appends to is released only when it is
+    // complete, whatever the next launch streams before its own wait.
+    pdl_wait_primary();
     const int lane = threadIdx.x & 31;
     const uint64_t item = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (item >= 2ull * rows) return;
@@ -249,10 +253,10 @@ cudaError_t launch_quant_append(const PpKvArena& a, const void* k_new, const voi
                                 const uint32_t* offsets, uint32_t commit, uint32_t* status, cudaStream_t stream) {
     const uint64_t warps = 2ull * a.rows;
     const uint32_t grid = (uint32_t)((warps + 7) / 8);
+    cudaError_t e;
 #define PP_APPEND(D, T)                                                                                       \
-    quant_append_kernel<D, T><<<grid, 256, 0, stream>>>((const T*)k_new, (const T*)v_new, a.rows, a.heads,     \
-                                                        a.capacity, offsets, commit, a.k, a.v, a.k_scale,      \
-                                                        a.v_scale, status)
+    e = launch_pdl(quant_append_kernel<D, T>, dim3(grid), dim3(256), stream, (const T*)k_new, (const T*)v_new,    \
+                   a.rows, a.heads, a.capacity, offsets, commit, a.k, a.v, a.k_scale, a.v_scale, status)
     if (a.head_dim == 128) {
         if (dtype == PP_DTYPE_F32) PP_APPEND(128, float);
         else PP_APPEND(128, __nv_bfloat16);
@@ -261,7 +265,7 @@ cudaError_t launch_quant_append(const PpKvArena& a, const void* k_new, const voi
         else PP_APPEND(64, __nv_bfloat16);
     }
 #undef PP_APPEND
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, uint64_t rows, uint32_t d, int round_bf16,
