@@ -39,8 +39,9 @@ WORKLOADS = {
     # name: branches per GPU, heads, head_dim, context, layers, description
     "cfg1": dict(branches=32, heads=16, d=128, ctx=4096, layers=24,
                  desc="BASELINE config 1: 32 branches x 16 heads x d128, context 4096, 24 layer caches, bf16 q/out"),
-    "cfg4": dict(branches=8, heads=16, d=128, ctx=16384, layers=4,
-                 desc="BASELINE config 4 shape: 8 branches x 16 heads x d128, context 16384, 4 layer caches"),
+    "cfg4": dict(branches=8, heads=16, d=128, ctx=16384, layers=4, dist="student_t",
+                 desc="BASELINE config 4: 8 branches x 16 heads x d128, context 16384, 4 layer caches, K/V "
+                      "Student-t(3) x 0.7 with 1% of channels x 8"),
     # the full synthetic decoder step (per GPU: 16 branches; the box: 128 branches on 8 GPUs)
     "cfg3": dict(branches=16, heads=16, d=128, ctx=2048, layers=24, width=2048, ffn=5632,
                  desc="BASELINE config 3: synthetic decoder (24 layers, width 2048, 16x128 heads, SwiGLU 5632, "
@@ -878,10 +879,24 @@ def main() -> int:
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     caches = []
+    def draw():
+        x = torch.randn(rows, L, D, device=dev, generator=gen)
+        if w.get("dist") == "student_t":
+            # Student-t(3) = z / sqrt(chi2(3) / 3), times 0.7; 1 % of the channels (at least one) x 8
+            chi = torch.zeros_like(x)
+            for _ in range(3):
+                chi.add_(torch.randn(rows, L, D, device=dev, generator=gen).square_())
+            x.div_(chi.div_(3).sqrt_()).mul_(0.7)
+            del chi
+            loud = torch.rand(D, device=dev, generator=gen) < 0.01
+            loud[int(torch.randint(0, D, (1,), device=dev, generator=gen))] = True
+            x[:, :, loud] *= 8
+        return x
+
     for _ in range(layers):
         kv = []
         for _ in range(2):
-            x = torch.randn(rows, L, D, device=dev, generator=gen)
+            x = draw()
             kv.append(ops.quantize(x, check_finite=False))
             del x
         caches.append((kv[0][0], kv[1][0], kv[0][1], kv[1][1]))
