@@ -591,8 +591,24 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                 meta->seg_begin = s_begin;
                 meta->seg_count = s_end - s_begin;
                 meta->n_orphans = n_orphans;
-                const uint32_t bytes = nbox * C::BOX * C::ROW * 2u + 2u * C::SC_BYTES + (first ? q_bytes : 0u);
+                // q goes with a segment's first stage only when the consumers read it
+                // there: the CTA's first segment, and segments past the q splits
+                // prepared at kernel start (the others would only make the stage
+                // wait for one more copy).  It is issued before the K/V copies.
+                const uint32_t rel = s - s_begin;
+                const bool load_q = first && (rel == 0 || rel >= (uint32_t)C::QSLOTS);
+                const uint32_t bytes = nbox * C::BOX * C::ROW * 2u + 2u * C::SC_BYTES + (load_q ? q_bytes : 0u);
                 mbar_arrive_expect_tx(&full[slot], bytes);
+                if (load_q) {
+                    const unsigned char* qrow =
+                        reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * args.q_stride * sizeof(QT);
+                    if (waited) {
+                        bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
+                    } else {
+                        pend_slot[pend_n] = slot;
+                        pend_src[pend_n++] = qrow;
+                    }
+                }
                 if constexpr (!C::SCALED) {
                     // float rows: 3-D maps {channel, token, row}, one copy per 128-byte panel
                     constexpr int PX = 128 / C::ELEM;  // channels per panel
@@ -641,16 +657,6 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                 for (int b = 0; b < C::SC_BOXES; ++b) {  // int8 only (no boxes for float rows)
                     tma_load_1d(st + C::OFF_KS + b * C::SC_BOX * 4, &map_ks, &full[slot], (int32_t)(ksx + b * C::SC_BOX));
                     tma_load_1d(st + C::OFF_VS + b * C::SC_BOX * 4, &map_vs, &full[slot], (int32_t)(vsx + b * C::SC_BOX));
-                }
-                if (first) {
-                    const unsigned char* qrow =
-                        reinterpret_cast<const unsigned char*>(args.q) + (uint64_t)sd.row * args.q_stride * sizeof(QT);
-                    if (waited) {
-                        bulk_load(st + C::OFF_Q, qrow, q_bytes, &full[slot]);
-                    } else {
-                        pend_slot[pend_n] = slot;
-                        pend_src[pend_n++] = qrow;
-                    }
                 }
             }
         }
