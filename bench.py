@@ -46,6 +46,10 @@ WORKLOADS = {
     "cfg3": dict(branches=16, heads=16, d=128, ctx=2048, layers=24, width=2048, ffn=5632,
                  desc="BASELINE config 3: synthetic decoder (24 layers, width 2048, 16x128 heads, SwiGLU 5632, "
                       "RMSNorm, RoPE 10000, random bf16 weights, int8 KV), 16 branches per GPU at context 2048"),
+    # bulk encode: one layer's K and V quantized to int8 codes + scales (int8_kv_ops::quantize, row a2)
+    "encode": dict(branches=32, heads=16, d=128, ctx=4096, layers=1, kv="bf16",
+                   desc="encode: one cfg1 layer's K and V (512 rows x 4096 x d128, bf16 in) quantized per (token, "
+                        "head) to int8 codes + f32 scales"),
     # the prefill path: one layer's whole int8 history back to bf16 (int8_cache.rs:363-371)
     "prefill": dict(branches=32, heads=16, d=128, ctx=4096, layers=1,
                     desc="prefill dequant: one cfg1 layer's int8 K and V (512 rows x 4096 x d128) to bf16"),
@@ -211,6 +215,37 @@ def cpu_reference(w, steps: int, warmup: int, sample_branches: int, threads: int
                       f"per step, {len(times)} timed steps, oracle/int8kv_oracle.c (reference arithmetic restated)"}
 
 
+def cpu_encode_reference(w, steps: int, warmup: int, sample_branches: int, threads: int, budget_s: float) -> dict:
+    """The reference quantizer restated on the CPU (oracle/int8kv_oracle.c:
+    int8_kv_ops.rs:13-21, one thread), timed on a bounded sample: the K of
+    `sample_branches` branches of one layer per step."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    rows, L, D = sample_branches * w["heads"], w["ctx"], w["d"]
+    g = np.random.Generator(np.random.PCG64(1))
+    x = g.standard_normal((rows * L, D), dtype=np.float32)
+    bf16 = w.get("kv", "bf16") == "bf16"
+    if bf16:
+        x = (x.view(np.uint32) >> 16).astype(np.uint16)
+    per_call = rows * L * D * ((2 if bf16 else 4) + 1) + rows * L * 4
+    for _ in range(max(0, warmup)):
+        oracle.quantize(x, D)
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        oracle.quantize(x, D)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    mean = sum(times) / len(times)
+    return {"value": per_call / mean / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"K of {sample_branches} branches x {w['heads']} heads x ctx {L} x d{D} "
+                      f"({'bf16' if bf16 else 'f32'} in) per step, {len(times)} timed steps, one thread, "
+                      f"oracle/int8kv_oracle.c (reference quantizer restated)"}
+
+
 def cpu_float_reference(w, steps: int, warmup: int, sample_branches: int, threads: int, budget_s: float) -> dict:
     """The float-KV attention arithmetic restated on the CPU
     (oracle/float_attn_oracle.c), timed on a bounded sample: `sample_branches`
@@ -250,14 +285,15 @@ def run_reference_arm(args, w) -> int:
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    ref = cpu_float_reference if args.workload == "float" else cpu_reference
+    ref = {"float": cpu_float_reference, "encode": cpu_encode_reference}.get(args.workload, cpu_reference)
     cb = ref(w, args.steps, args.warmup, sample_branches=1, threads=threads, budget_s=120.0)
     n = args.gpus
     line = {
         "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
         "impl": "reference", "value": cb["value"], "unit": "GB/s", "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": ("bf16 KV" if args.workload == "float" else "int8 KV") + ", f32 accumulate",
+        "dtype": {"float": "bf16 KV, f32 accumulate", "encode": w.get("kv", "bf16") + " in, int8 codes + f32 scales out"}
+        .get(args.workload, "int8 KV, f32 accumulate"),
         "data": "synthetic (seeded)",
         "config": {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"],
                    "heads": w["heads"], "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"],
@@ -588,6 +624,80 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
 
 
 
+def run_encode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """Bulk encode (int8_kv_ops::quantize, int8_kv_ops.rs:11-27; the CUDA
+    branch pp_i8_scale + pp_i8_pack, int8_kv.cu:8-18): one layer's K and V
+    quantized per (token, head) row, bf16 (default) or f32 in; no collective."""
+    rows, L, D = w["branches"] * w["heads"], w["ctx"], w["d"]
+    n = rows * L
+    t = torch.bfloat16 if w.get("kv", "bf16") == "bf16" else torch.float32
+    elem = 2 if t == torch.bfloat16 else 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    xs = [torch.randn(n, D, device=dev, generator=gen).to(t) for _ in range(2)]
+    codes = [torch.empty(n, D, dtype=torch.uint8, device=dev) for _ in range(2)]
+    scales = [torch.empty(n, dtype=torch.float32, device=dev) for _ in range(2)]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib, N = pp._native.lib, pp._native
+    P = lambda t_: C.c_void_p(t_.data_ptr())  # noqa: E731
+    sp = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    dt = N.DTYPE_BF16 if t == torch.bfloat16 else N.DTYPE_F32
+
+    def step():
+        for j in range(2):
+            N.check(lib.pp_b200_quantize(P(xs[j]), dt, n, D, P(codes[j]), P(scales[j]), P(status), sp))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise SystemExit(f"device status after warm-up: {N.status_message(int(status.item()))}")
+    stream = torch.cuda.current_stream(dev)
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    tt = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+    ms_step = float(tt.item())
+    per_call = n * D * (elem + 1) + n * 4
+    per_step = 2 * per_call
+    peak, peak_kind = load_peaks()
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_encode_reference(w, steps=3, warmup=1, sample_branches=1, threads=1, budget_s=20.0)
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": world * per_step / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": f"{'bf16' if elem == 2 else 'f32'} in, int8 codes + f32 scales out",
+            "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": "encode", "desc": w["desc"], "rows": rows, "context": L, "head_dim": D,
+                       "input": "bf16" if elem == 2 else "f32",
+                       "l2": f"{per_step / 1e9:.2f} GB per step, larger than L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": per_step / (ms_local * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": per_step / (ms_local * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                         "per_launch_bytes": per_call, "per_launch_ms": ms_local / 2,
+                         "timed": "two quantize calls (K, V) per step, CUDA events"},
+            "clocks": clocks.summary(), "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
 def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     """The prefill dequant path: one layer's int8 K and V histories back to
     bf16 (Int8LayerCache::prefill_prefix, int8_cache.rs:363-371), 1.6 GB of
@@ -829,7 +939,8 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="cfg3: launch the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-prefetch", action="store_true", help="never stream history before the previous kernel ends")
-    ap.add_argument("--kv-dtype", choices=["bf16", "f32"], default=None, help="float workload: K/V element type")
+    ap.add_argument("--kv-dtype", choices=["bf16", "f32"], default=None,
+                    help="float workload: K/V element type; encode: input element type")
     ap.add_argument("--gemm", choices=["rows", "cublas"], default="cublas",
                     help="cfg3: projections by cuBLAS (default) or the decode-row GEMM")
     args = ap.parse_args()
@@ -864,6 +975,8 @@ def main() -> int:
         return run_cfg3(args, w, pp, pg, world, rank, local, dev)
     if args.workload == "prefill":
         return run_prefill(args, w, pp, pg, world, rank, local, dev)
+    if args.workload == "encode":
+        return run_encode(args, w, pp, pg, world, rank, local, dev)
     if args.workload == "float":
         return run_float(args, w, pp, pg, world, rank, local, dev)
 

@@ -39,6 +39,63 @@ def test_quantize_bit_exact_vs_oracle(pp, oracle, cuda, d, dtype, seed):
     assert np.array_equal(u32(scales.cpu().numpy().reshape(rows)), u32(ref_scales))
 
 
+def _near_tie_rows(d, bf16, seed, rows=512):
+    """Rows whose elements sit on, and a few units in the last place around,
+    x / s = k + 0.5 for every code k, where the quotient's rounding decides
+    the code.  Element 0 is the row maximum that sets s.  bf16 rows use
+    power-of-two scales, so the ties are exact; f32 rows use arbitrary scales."""
+    g = np.random.Generator(np.random.PCG64(900 + seed))
+    out = np.zeros((rows, d), np.float32)
+    for r in range(rows):
+        if bf16:
+            s = np.float32(2.0 ** int(g.integers(-30, 12)))
+            m = np.float32(127) * s
+        else:
+            m = np.float32(127 * g.uniform(1e-3, 1e2))
+            s = np.float32(np.float32(m) / np.float32(127))
+        k = g.integers(-127, 127, d - 1)
+        x = (k.astype(np.float32) + np.float32(0.5)) * s
+        if bf16:
+            bits = (x.view(np.uint32) >> 16).astype(np.int64) + g.integers(-1, 2, d - 1)
+            x = (bits.astype(np.uint32) << 16).view(np.float32)
+        else:
+            x = (x.view(np.int32) + g.integers(-3, 4, d - 1).astype(np.int32)).view(np.float32)
+        out[r, 0] = m if g.integers(0, 2) else -m
+        out[r, 1:] = np.clip(x, -np.abs(m), np.abs(m))
+    return out
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_quantize_near_ties_bit_exact(pp, oracle, cuda, d, dtype):
+    """Codes of elements whose quotient x / s falls on or next to a half-integer,
+    by the bulk quantizer and by quantize-and-append, equal the oracle's (exact
+    f32 division, round half to even)."""
+    bf16 = dtype == torch.bfloat16
+    x = _near_tie_rows(d, bf16, d + bf16)
+    rows = x.shape[0]
+    if bf16:
+        bits = K.to_bf16_bits(x)
+        assert np.array_equal((bits.astype(np.uint32) << 16).view(np.float32), x)  # the rows are bf16 values
+        xt = to_dev(bits.view(np.int16), cuda).view(torch.bfloat16)
+        ref_codes, ref_scales = oracle.quantize(bits, d)
+    else:
+        xt = to_dev(x, cuda)
+        ref_codes, ref_scales = oracle.quantize(x)
+    codes, scales = pp.int8_kv_ops.quantize(xt.reshape(1, rows, d))
+    assert np.array_equal(codes.cpu().numpy().reshape(rows, d), ref_codes)
+    assert np.array_equal(u32(scales.cpu().numpy().reshape(rows)), u32(ref_scales))
+    # the same rows through quantize-and-append (one token per (branch, head) row)
+    heads = 16
+    arena = pp.kv_cache.Int8KvArena.zeros(rows // heads, heads, d, 4, cuda)
+    offs = torch.full((rows // heads,), 2, dtype=torch.int32, device=cuda)
+    arena.append(xt, xt, offs)
+    torch.cuda.synchronize()
+    assert np.array_equal(arena.k[:, 2].cpu().numpy(), ref_codes)
+    assert np.array_equal(arena.v[:, 2].cpu().numpy(), ref_codes)
+    assert np.array_equal(u32(arena.k_scale[:, 2].cpu().numpy()), u32(ref_scales))
+
+
 def test_quantize_matches_reference_kernel_codes(pp, cuda, golden):
     """Codes and scales equal the reference CUDA kernels' (pp_i8_scale/pack)."""
     ops = pp.int8_kv_ops
