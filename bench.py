@@ -1,6 +1,7 @@
 """Benchmark of the int8 historical-KV decode step on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1|cfg2|cfg3|cfg4|prefill|float]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg1|cfg2|cfg3|cfg4|prefill|encode|float]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1, one rank per GPU)
 
 Workload cfg1 (the one the headline metric is quoted
