@@ -935,6 +935,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
     ap.add_argument("--layers", type=int, default=0, help="override the number of layer caches")
+    ap.add_argument("--head-dim", type=int, choices=[64, 128], default=0,
+                    help="override the head size (64: the reference model's own)")
     ap.add_argument("--split", type=int, default=0, help="fixed split size in tokens (0: automatic)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -950,6 +952,11 @@ def main() -> int:
         w["layers"] = args.layers
     if args.kv_dtype:
         w["kv"] = args.kv_dtype
+    if args.head_dim:
+        if args.workload == "cfg3":
+            raise SystemExit("--head-dim does not apply to the decoder workload")
+        w["d"] = args.head_dim
+        w["desc"] += f" (head_dim overridden to {args.head_dim})"
     if args.impl == "reference":
         return run_reference_arm(args, w)
 
@@ -1086,7 +1093,8 @@ def main() -> int:
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
-                traffic = json.load(f).get(args.workload)
+                # the captured figure is for the workload's own head size
+                traffic = None if args.head_dim else json.load(f).get(args.workload)
         except Exception:
             traffic = None
 
