@@ -566,7 +566,16 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
         for (uint32_t s = s_begin; s < s_end && ok; ++s) {
             const SegDesc sd = next;
             if (s + 1 < s_end) next = segs[s + 1];
-            for (uint32_t t = sd.t0; t < sd.t1; t += C::T, ++it) {
+            for (uint32_t t = sd.t0, n = 0; t < sd.t1; t += n, ++it) {
+                // T tokens per stage, except that a remainder which would leave the
+                // segment's last stage less than half full is split with the stage
+                // before it into two stages of about equal size (whole 16-token
+                // units first): a nearly empty stage holds a ring slot while the
+                // consumers get through it at once and then wait for the next
+                const uint32_t rem = sd.t1 - t;
+                n = rem <= (uint32_t)C::T ? rem
+                    : rem < (uint32_t)(C::T + C::T / 2) ? ((rem + 1) / 2 + C::BOX - 1) / C::BOX * C::BOX
+                                                        : (uint32_t)C::T;
                 const uint32_t slot = it % C::STAGES, ph = (it / C::STAGES) & 1u;
                 if (it == (uint32_t)C::STAGES) release_q();  // the ring is full: q before anything else
                 if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, kWaitLimitNs)) {
@@ -574,12 +583,11 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                     break;
                 }
                 unsigned char* st = smem + slot * C::STAGE_BYTES;
-                const uint32_t n = min((uint32_t)C::T, sd.t1 - t);
                 const uint32_t nbox = (n + C::BOX - 1) / C::BOX;
                 const uint32_t tok = sd.row * args.capacity + t;
                 const uint32_t ksx = (args.ks_mis + tok) & ~3u, vsx = (args.vs_mis + tok) & ~3u;
                 StageMeta* meta = reinterpret_cast<StageMeta*>(st + C::OFF_META);
-                const bool first = t == sd.t0, last = t + C::T >= sd.t1;
+                const bool first = t == sd.t0, last = t + n >= sd.t1;
                 meta->row = sd.row;
                 meta->t = t;
                 meta->nvalid = n;
