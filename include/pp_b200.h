@@ -4,7 +4,7 @@
  * This is the drop-in boundary for the reference's `int8_kv_ops` module
  * (app/src/model/int8_kv_ops.rs), whose CUDA branches are Candle CustomOps
  * launched through cudarc.  A Rust `extern "C"` crate binds these entry points
- * in place of those CustomOps; INTEGRATION.md shows the binding.
+ * in place of those CustomOps.
  *
  * Conventions (style of app/native/aten_hip/cpp/painter_ffi.h:20-25):
  *   - every entry point returns an int32 status:
