@@ -184,6 +184,35 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+def attention_config(args, w, world: int) -> dict:
+    """The `config` object of the cfg1 / cfg4 attention lines (both arms)."""
+    return {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"], "heads": w["heads"],
+            "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"], "split_tokens": args.split,
+            "parallelism": f"branch shards x{world} (no collective in the step)",
+            "l2": "inputs larger than L2 (each layer cache > 126 MB), no flush"}
+
+
+def per_rank(pg, dev, ms_local: float, steps: int, clocks: "ClockSampler") -> list:
+    """Every rank's own device time per step and its median SM clock during
+    the timed region, gathered to every rank (one all_gather, outside the
+    timed region).  time x clock per rank separates a slower clock (shared
+    power budget) from a rank that did more work or waited on its host."""
+    c = clocks.summary()
+    mine = torch.tensor([ms_local / max(1, steps), float(c["sm_mhz"] or 0.0), float(clocks.reasons)],
+                        dtype=torch.float64, device=dev)
+    if pg is None:
+        rows = [mine]
+    else:
+        rows = [torch.empty_like(mine) for _ in range(pg.get_world_size())]
+        pg.all_gather(rows, mine)
+    out = []
+    for r, t in enumerate(rows):
+        ms, mhz, bits = (float(x) for x in t.tolist())
+        names = [n for bit, n in ClockSampler.REASONS.items() if int(bits) & bit and n != "gpu_idle"]
+        out.append({"rank": r, "ms_per_step": ms, "sm_mhz": mhz or None, "reasons": names})
+    return out
+
+
 def cpu_reference(w, steps: int, warmup: int, sample_branches: int, threads: int, budget_s: float) -> dict:
     """The reference arithmetic restated on the CPU (oracle/), timed on a
     bounded sample of the same workload: `sample_branches` branches of one
@@ -296,7 +325,9 @@ def run_reference_arm(args, w) -> int:
         "dtype": {"float": "bf16 KV, f32 accumulate", "encode": w.get("kv", "bf16") + " in, int8 codes + f32 scales out"}
         .get(args.workload, "int8 KV, f32 accumulate"),
         "data": "synthetic (seeded)",
-        "config": {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"],
+        # the same workload description as this repository's arm (what was sampled is in cpu_baseline)
+        "config": attention_config(args, w, n) if args.workload in ("cfg1", "cfg4") else
+                  {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"],
                    "heads": w["heads"], "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"],
                    "parallelism": "replicas only (host cores)"},
         "cpu_baseline": cb,
@@ -387,6 +418,7 @@ def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
     barrier()
     ms_local = start.elapsed_time(end)
+    ranks = per_rank(pg, dev, ms_local, steps, clocks)
     ms_step = max_over_ranks(ms_local) / steps
 
     # bytes: attention reads every branch's whole history once, plus q, out and the append
@@ -478,7 +510,7 @@ def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_step,
                          "per_launch_ms": ms_local / steps,
                          "timed": "timed region / steps: append + plan + attention per step (CUDA events)"},
-            "clocks": clocks.summary(),
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
             "e2e": e2e,
             "gpu_launches": steps * (4 if args.split else 3),  # append, plan, attention (+ combine)
             "cpu_baseline": cpu,
@@ -557,6 +589,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
     barrier()
     ms_local = start.elapsed_time(end)
+    ranks = per_rank(pg, dev, ms_local, steps, clocks)
     ms_step = max_over_ranks(ms_local) / steps
     tokens_per_s = world * B / (ms_step * 1e-3)
 
@@ -611,7 +644,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_step,
                          "per_launch_ms": ms_local / steps,
                          "timed": "whole decode step (weights + int8 history bytes) per step, CUDA events"},
-            "clocks": clocks.summary(),
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
             "e2e": e2e,
             # plan; per layer 2 rmsnorm, qkv_rope_append, attention, swiglu (+ 4 decode-row GEMMs); final rmsnorm
             "gpu_launches": steps * (1 + cfg.layers * (5 + (4 if model.rows_gemm else 0)) + 1),
@@ -667,6 +700,7 @@ def run_encode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     if pg is not None:
         pg.barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
+    ranks = per_rank(pg, dev, ms_local, 1, clocks)
     tt = torch.tensor([ms_local], dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(tt, op=pg.ReduceOp.MAX)
@@ -691,7 +725,7 @@ def run_encode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "frac": per_step / (ms_local * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
                          "per_launch_bytes": per_call, "per_launch_ms": ms_local / 2,
                          "timed": "two quantize calls (K, V) per step, CUDA events"},
-            "clocks": clocks.summary(), "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": cpu,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0, "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -737,6 +771,7 @@ def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     if pg is not None:
         pg.barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
+    ranks = per_rank(pg, dev, ms_local, 1, clocks)
     t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -755,7 +790,7 @@ def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "frac": per_step / (ms_local * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
                          "per_launch_bytes": per_step / 2, "per_launch_ms": ms_local / 2,
                          "timed": "two dequantize calls (K, V) per step, CUDA events"},
-            "clocks": clocks.summary(), "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": None,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0, "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -827,6 +862,7 @@ def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
     barrier()
     ms_local = e0.elapsed_time(e1)
+    ranks = per_rank(pg, dev, ms_local, args.steps, clocks)
     ms_step = max_over_ranks(ms_local) / args.steps
     call_ms = ms_local / (args.steps * layers)
     per_call = rows * L * 2 * D * elem + rows * D * 4 + rows * D * 4
@@ -916,7 +952,7 @@ def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "peak_kind": peak_kind, "per_launch_bytes": per_call, "per_launch_ms": call_ms,
                          "timed": "timed region / attention calls (CUDA events on the launching stream): "
                                   "attn_kernel over float rows, with the plan amortised over the step"},
-            "clocks": clocks.summary(), "e2e": e2e,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0, "e2e": e2e,
             "gpu_launches": args.steps * (1 + (2 if args.split else 1) * layers),
             "cpu_baseline": cpu,
         }
@@ -1071,6 +1107,7 @@ def main() -> int:
         torch.cuda.synchronize()
     barrier()
     ms_total = ms_local = start.elapsed_time(end)
+    ranks = per_rank(pg, dev, ms_local, args.steps, clocks)
     t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -1178,10 +1215,7 @@ def main() -> int:
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 KV (bf16-rounded dequant), bf16 q/out, f32 accumulate", "data": "synthetic (seeded)",
-            "config": {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": B, "heads": H,
-                       "head_dim": D, "context": L, "layers": layers, "split_tokens": args.split,
-                       "parallelism": f"branch shards x{world} (no collective in the step)",
-                       "l2": "inputs larger than L2 (each layer cache > 126 MB), no flush"},
+            "config": attention_config(args, w, world),
             "tokens_per_s": tokens_per_s,
             "percent_of_peak": 100.0 * value / (world * peak),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -1189,7 +1223,7 @@ def main() -> int:
                          "per_launch_bytes": per_call, "per_launch_ms": call_ms,
                          "timed": "timed region / attention calls (CUDA events on the launching stream): "
                                   "attn_kernel, with the plan amortised over the step"},
-            "clocks": clocks.summary(),
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
             "e2e": e2e,
             # per step: one plan, then per layer the attention kernel (+ the combine kernel with fixed splits)
             "gpu_launches": args.steps * (1 + (2 if args.split else 1) * layers),

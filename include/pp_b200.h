@@ -186,6 +186,9 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
  * GPU (different streams, or several host threads) race and must be
  * serialised by the caller.  The first call on each device looks up the
  * array's device address; make that first call before any stream capture.
+ * The address is looked up again, by the next call, when the device's
+ * context has been made anew (after cudaDeviceReset): that call too must come
+ * before any capture.
  * Nothing is allocated: no cudaMalloc, cudaFree or allocating library call. */
 int32_t pp_b200_decode_attention_static(const PpKvArena* arena, const PpAttnParams* params, const void* q,
                                         const float* scratch_k, const float* scratch_v,

@@ -43,6 +43,7 @@ int32_t cuda_fail(cudaError_t e, const char* what) {
 
 struct DeviceInfo {
     bool ready = false;
+    unsigned long long ctx_id = 0;  // context the kernel attributes were set in
     int num_sms = 0;
     int major = 0;
 };
@@ -56,9 +57,14 @@ int32_t device_info(DeviceInfo& out) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (dev < 0 || dev >= 64) return fail(PP_STATUS_PRECONDITION, "device ordinal %d out of range", dev);
+    unsigned long long ctx = 0;
+    if (pp::current_context_id(&ctx) != PP_STATUS_OK) return PP_STATUS_PRECONDITION;
     std::lock_guard<std::mutex> lock(g_dev_mu);
     DeviceInfo& d = g_dev[dev];
-    if (!d.ready) {
+    // kernel attributes belong to the context: a context made anew (after
+    // cudaDeviceReset, or a released and re-created primary context) needs them again
+    if (!d.ready || d.ctx_id != ctx) {
+        d.ready = false;
         int minor = 0;
         if ((e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
             return cuda_fail(e, "cudaDeviceGetAttribute");
@@ -80,11 +86,16 @@ int32_t device_info(DeviceInfo& out) {
                 return fail(PP_STATUS_PRECONDITION, "CUDA_ERROR_NOT_SUPPORTED: cuTensorMapEncodeTiled unavailable");
             g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
         }
+        d.ctx_id = ctx;
         d.ready = true;
     }
     out = d;
     return PP_STATUS_OK;
 }
+
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
@@ -285,6 +296,33 @@ namespace pp {
 int32_t fail_msg(int32_t status, const char* msg) {
     g_last_error = msg;
     return status;
+}
+
+int32_t current_context_id(unsigned long long* id) {
+    // the driver's context calls, reached through the runtime (the library
+    // links only the runtime); cudaFree(nullptr) makes the primary context current
+    std::call_once(g_ctx_once, [] {
+        void* a = nullptr;
+        void* b = nullptr;
+        cudaDriverEntryPointQueryResult qa{}, qb{};
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &a, 4000, cudaEnableDefault, &qa) == cudaSuccess &&
+            qa == cudaDriverEntryPointSuccess)
+            g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(a);
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &b, 12000, cudaEnableDefault, &qb) == cudaSuccess &&
+            qb == cudaDriverEntryPointSuccess)
+            g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(b);
+    });
+    if (!g_ctx_current || !g_ctx_id)
+        return fail(PP_STATUS_PRECONDITION, "CUDA_ERROR_NOT_SUPPORTED: cuCtxGetCurrent / cuCtxGetId unavailable");
+    CUcontext ctx = nullptr;
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx) {
+        cudaError_t e = cudaFree(nullptr);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFree(nullptr) (context set-up)");
+        if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx)
+            return fail(PP_STATUS_UNCERTAIN, "EXECUTION_UNCERTAIN: no current CUDA context");
+    }
+    if (g_ctx_id(ctx, id) != CUDA_SUCCESS) return fail(PP_STATUS_UNCERTAIN, "EXECUTION_UNCERTAIN: cuCtxGetId failed");
+    return PP_STATUS_OK;
 }
 }  // namespace pp
 

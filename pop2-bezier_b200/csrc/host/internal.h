@@ -175,4 +175,10 @@ cudaError_t launch_rows_gemm_pack(const void* w, uint64_t ldw, uint32_t n, uint3
 // Records `msg` as the calling thread's last error and returns `status`.
 int32_t fail_msg(int32_t status, const char* msg);
 
+// The unique ID of the calling thread's current CUDA context (the primary
+// context is made current if none is).  Per-context state (kernel attributes,
+// module symbol addresses) is cached against it: an ID that changed means the
+// context was made anew and that state must be set up again.
+int32_t current_context_id(unsigned long long* id);
+
 }  // namespace pp

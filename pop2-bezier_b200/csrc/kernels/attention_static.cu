@@ -22,28 +22,46 @@ constexpr size_t kStaticWorkspaceBytes = size_t(4) << 20;  // 4 MiB
 __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
 
 std::mutex g_static_mu;
-void* g_static_ptr[64] = {};  // device address of g_static_workspace, per device
+struct StaticAddress {
+    void* ptr = nullptr;
+    unsigned long long ctx_id = 0;  // the context the address was looked up in
+};
+StaticAddress g_static_addr[64];  // device address of g_static_workspace, per device
 
-// Looks up the array's device address on the current device once (host code
-// must not use the symbol itself as a device pointer).
-int32_t static_workspace(void** out) {
+// Looks up the array's device address (host code must not use the symbol
+// itself as a device pointer).  The address belongs to the context that loaded
+// the module: it is looked up once per context, and again when the device's
+// context was made anew (after cudaDeviceReset, or a released and re-created
+// primary context), when the module may have been loaded elsewhere.
+int32_t static_workspace(void** out, void* stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess)
         return pp::fail_msg(PP_STATUS_UNCERTAIN, "EXECUTION_UNCERTAIN: cudaGetDevice failed in decode_attention_static");
     if (dev < 0 || dev >= 64) return pp::fail_msg(PP_STATUS_PRECONDITION, "decode_attention_static: device ordinal out of range");
+    unsigned long long ctx = 0;
+    const int32_t s = pp::current_context_id(&ctx);
+    if (s != PP_STATUS_OK) return s;
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (!g_static_ptr[dev]) {
+    StaticAddress& a = g_static_addr[dev];
+    if (!a.ptr || a.ctx_id != ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_static_workspace);
         if (e != cudaSuccess || !p) {
-            char msg[256];
-            snprintf(msg, sizeof msg, "decode_attention_static: cudaGetSymbolAddress failed: %s", cudaGetErrorName(e));
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            const bool capturing = cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cap) == cudaSuccess &&
+                                   cap != cudaStreamCaptureStatusNone;
+            char msg[320];
+            snprintf(msg, sizeof msg, "decode_attention_static: cudaGetSymbolAddress failed: %s%s", cudaGetErrorName(e),
+                     capturing ? " (the stream is being captured: make the first call on this device, and the first "
+                                 "after a context reset, before any capture)"
+                               : "");
             return pp::fail_msg(PP_STATUS_PRECONDITION, msg);
         }
-        g_static_ptr[dev] = p;
+        a.ptr = p;
+        a.ctx_id = ctx;
     }
-    *out = g_static_ptr[dev];
+    *out = a.ptr;
     return PP_STATUS_OK;
 }
 
@@ -69,7 +87,7 @@ extern "C" int32_t pp_b200_decode_attention_static(const PpKvArena* arena, const
         return pp::fail_msg(PP_STATUS_PRECONDITION, msg);
     }
     void* ws = nullptr;
-    const int32_t s = static_workspace(&ws);
+    const int32_t s = static_workspace(&ws, stream);
     if (s != PP_STATUS_OK) return s;
     return pp_b200_decode_attention(arena, params, q, scratch_k, scratch_v, lengths, out, ws, kStaticWorkspaceBytes,
                                     status, stream);

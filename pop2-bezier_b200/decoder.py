@@ -284,11 +284,18 @@ class SyntheticDecoder:
             return rows_gemm(x, self.packed[li][name], w.shape[0], out=out, status=self.status)
         return torch.matmul(x, w.t())
 
-    def step(self, x: torch.Tensor, past: torch.Tensor, positions: torch.Tensor | None = None) -> torch.Tensor:
+    def step(self, x: torch.Tensor, past: torch.Tensor, positions: torch.Tensor | None = None, *,
+             commit: bool = True, probe=None) -> torch.Tensor:
         """One decode token for every branch.  x [branches, width] (the input
         embedding), past u32/i32 [branches] (tokens already in each branch's
         cache; the new K/V go to slot past[b]); returns the final-normed
-        hidden state [branches, width].  x is consumed (used as the residual)."""
+        hidden state [branches, width].  x is consumed (used as the residual).
+        commit=False is the reference's partial query (int8_cache.rs:305-310):
+        slot past[b] receives the placeholder (zero codes, scale 1) and the
+        attention still sees the current token through the f32 scratch.
+        probe(layer, q, scratch_k, scratch_v, arena, attention_out), when
+        given, is called after each layer's attention is enqueued (eager
+        steps only; it may synchronise and read the tensors)."""
         cfg, b = self.cfg, self._buf
         H, d = cfg.heads, cfg.head_dim
         pos = past if positions is None else positions
@@ -300,14 +307,16 @@ class SyntheticDecoder:
         for li, (L, arena) in enumerate(zip(self.layers, self.arenas)):
             rmsnorm(xr, L["norm1"], residual=residual, x_sum=xr if residual is not None else None, out=b["normed"])
             qkv = self._linear(b["normed"], li, "qkv", b["qkv"])
-            qkv_rope_append(qkv, L["rope"], pos, arena, past, cfg.max_context, q_out=b["q"], scratch_k=b["sk"],
-                            scratch_v=b["sv"], status=self.status)
+            qkv_rope_append(qkv, L["rope"], pos, arena, past, cfg.max_context, commit=commit, q_out=b["q"],
+                            scratch_k=b["sk"], scratch_v=b["sv"], status=self.status)
             # qkv_rope_append writes slot past[b], after the history: the attention may stream
             # the history while it finishes
             ops.decode_attention(b["q"], arena.k, arena.v, arena.k_scale, arena.v_scale, past, H,
                                  scratch_k=b["sk"], scratch_v=b["sv"], out_dtype=self.dtype,
                                  workspace=self.workspace, plan_ready=True, status=self.status, out=b["att"],
                                  prefetch_history=self.prefetch)
+            if probe is not None:
+                probe(li, b["q"], b["sk"], b["sv"], arena, b["att"])
             proj = self._linear(b["att"].view(self.branches, H * d), li, "proj", b["proj"])
             rmsnorm(xr, L["norm2"], residual=proj, x_sum=xr, out=b["normed"])
             gate_up = self._linear(b["normed"], li, "gate_up", b["gate_up"])

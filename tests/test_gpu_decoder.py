@@ -247,3 +247,40 @@ def test_decoder_step_without_history_prefetch_gives_the_same_bits(pp, cuda):
     without = m.step(x.clone(), past).clone()
     torch.cuda.synchronize()
     assert torch.equal(with_prefetch.view(torch.int16), without.view(torch.int16))
+
+
+def test_cfg3_every_layer_attention_vs_oracle(pp, oracle, cuda):
+    """BASELINE config 3 at full size (24 layers, width 2048, 16 x 128 heads,
+    SwiGLU 5632, 16 branches at context 2048): one decode step, and after
+    each layer's attention the output of all 256 rows is checked against the
+    oracle on the same arena, query and f32 scratch token (reference mode:
+    the history of `past` int8 tokens plus the current token in f32)."""
+    import oracle as O
+
+    D = pp.decoder
+    cfg = D.DecoderConfig()  # 24 x 2048, 16 x 128, 5632
+    B, L0 = 16, 2048
+    m = D.SyntheticDecoder(cfg, branches=B, capacity=L0 + 8, device=cuda, seed=31)
+    m.fill_history(None, seed=32)
+    past = torch.full((B,), L0, dtype=torch.int32, device=cuda)
+    x = (torch.randn(B, cfg.width, device=cuda, generator=torch.Generator(device=cuda).manual_seed(33)) * 0.5)
+    seen = []
+
+    def probe(li, q, sk, sv, arena, att):
+        torch.cuda.synchronize()
+        ref = O.attention(q.float().cpu().numpy(), arena.k.cpu().numpy(), arena.v.cpu().numpy(),
+                          arena.k_scale.cpu().numpy(), arena.v_scale.cpu().numpy(), past.cpu().numpy(), cfg.heads,
+                          sk=sk.cpu().numpy(), sv=sv.cpu().numpy(), threads=O.max_threads())
+        got = att.float().cpu().numpy()
+        ref_b = O.bf16_round(ref)
+        mag = np.maximum(np.abs(ref_b), np.float32(2.0**-126))
+        ulp = np.exp2(np.floor(np.log2(mag)) - 7).astype(np.float32)
+        bad = np.abs(got - ref_b) > np.maximum(ulp, 1e-3)
+        assert not bad.any(), f"layer {li}: {bad.sum()} of {bad.size} attention outputs beyond one bf16 ulp"
+        seen.append(li)
+
+    out = m.step(x.to(torch.bfloat16), past, probe=probe)
+    torch.cuda.synchronize()
+    assert int(m.status.item()) == 0
+    assert seen == list(range(cfg.layers))
+    assert torch.isfinite(out.float()).all()

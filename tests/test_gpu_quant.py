@@ -234,9 +234,11 @@ def test_growth_copies_codes_and_scales_without_requantizing(pp, cuda):
 def test_cfg2_ragged_append_256_steps_codes_bit_exact(pp, oracle, cuda):
     """64 branches, 16 heads, d 128, initial lengths
     U[256, 8192], one bf16 N(0, 0.5^2) K/V token appended per branch per step
-    for 256 steps; the int8 codes and scales of every appended token are
-    checked bit-exactly against the oracle after every step, and the decode
-    attention of sampled rows against the oracle every 64 steps."""
+    for 256 steps.  After every step the int8 codes and scales of every
+    appended token are checked bit-exactly against the oracle; at the first
+    and last step and every 16th step the decode attention of all 1024 rows
+    is checked against the oracle over a host copy of the arena that the
+    checked appends keep up to date."""
     branches, heads, d = 64, 16, 128
     g = np.random.Generator(np.random.PCG64(2))
     lengths = g.integers(256, 8193, branches).astype(np.int64)
@@ -249,14 +251,16 @@ def test_cfg2_ragged_append_256_steps_codes_bit_exact(pp, oracle, cuda):
     arena.v.random_(0, 256, generator=tg)
     arena.k_scale.uniform_(0.005, 0.05, generator=tg)
     arena.v_scale.uniform_(0.005, 0.05, generator=tg)
+    mirror = [t.cpu().numpy() for t in (arena.k, arena.v, arena.k_scale, arena.v_scale)]
     lens_dev = torch.tensor(lengths, dtype=torch.int32, device=cuda)
-    ws = None
     row_idx = torch.arange(rows, device=cuda)
+    checked = 0
     for step in range(256):
         xk = (torch.randn(rows, d, device=cuda, generator=tg) * 0.5).to(torch.bfloat16)
         xv = (torch.randn(rows, d, device=cuda, generator=tg) * 0.5).to(torch.bfloat16)
         arena.append(xk, xv, lens_dev)
-        slot = lens_dev.repeat_interleave(heads).long()
+        slot_np = lens_dev.repeat_interleave(heads).cpu().numpy()
+        slot = torch.from_numpy(slot_np).to(cuda).long()
         got_k = arena.k[row_idx, slot].cpu().numpy()
         got_ks = arena.k_scale[row_idx, slot].cpu().numpy()
         got_v = arena.v[row_idx, slot].cpu().numpy()
@@ -267,14 +271,16 @@ def test_cfg2_ragged_append_256_steps_codes_bit_exact(pp, oracle, cuda):
         cv, sv = oracle.quantize(bv, d)
         assert np.array_equal(got_k, ck) and np.array_equal(got_v, cv), f"codes differ at step {step}"
         assert np.array_equal(u32(got_ks), u32(sk)) and np.array_equal(u32(got_vs), u32(sv))
+        r = np.arange(rows)
+        mirror[0][r, slot_np], mirror[1][r, slot_np] = ck, cv
+        mirror[2][r, slot_np], mirror[3][r, slot_np] = sk, sv
         lens_dev += 1
-        if step % 64 == 63:
+        if step == 0 or step % 16 == 15:
             q = torch.randn(rows, d, device=cuda, generator=tg).to(torch.bfloat16)
             out = arena.attention(q, lens_dev, out_dtype=torch.float32)
-            pick = np.array([0, 17, 333, 700, rows - 1])
-            lk = lens_dev.cpu().numpy()
-            qa = q.float().cpu().numpy()[pick]
-            sub = lambda t: t[torch.from_numpy(pick).to(cuda)].cpu().numpy()  # noqa: E731
-            ref = oracle.attention(qa, sub(arena.k), sub(arena.v), sub(arena.k_scale), sub(arena.v_scale),
-                                   lk[pick // heads], 1)
-            np.testing.assert_allclose(out.cpu().numpy()[pick], ref, rtol=2e-3, atol=1e-3)
+            ref = oracle.attention(q.float().cpu().numpy(), *mirror, lens_dev.cpu().numpy(), heads,
+                                   threads=oracle.max_threads())
+            got = out.cpu().numpy()
+            np.testing.assert_allclose(got, ref, rtol=2e-3, atol=1e-3, err_msg=f"step {step}")
+            checked += 1
+    assert checked == 17

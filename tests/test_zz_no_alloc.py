@@ -82,3 +82,53 @@ def test_static_scratch_rejects_geometry_beyond_its_size(pp, cuda):
     status = _static_call(pp, q, k, k, ks, ks, lens, heads, out, split=64)
     assert status == N.STATUS_PRECONDITION
     assert "static" in N.last_error() and "workspace" in N.last_error()
+
+
+def test_static_scratch_refuses_plan_reuse(pp, cuda):
+    """PP_ATTN_PLAN_READY would reuse a plan that another call may have
+    overwritten in the shared scratch: refused before any launch."""
+    ops, N = pp.int8_kv_ops, pp._native
+    k = torch.zeros(4, 64, 128, dtype=torch.uint8, device=cuda)
+    ks = torch.ones(4, 64, dtype=torch.float32, device=cuda)
+    q = torch.zeros(4, 128, dtype=torch.float32, device=cuda)
+    out = torch.zeros(4, 128, dtype=torch.float32, device=cuda)
+    lens = torch.full((1,), 64, dtype=torch.int32, device=cuda)
+    arena = ops.arena_struct(k, k, ks, ks, 4)
+    params = ops.attn_params(plan_ready=True)
+    st = N.lib.pp_b200_decode_attention_static(C.byref(arena), C.byref(params), ops._ptr(q), None, None,
+                                               ops._ptr(lens), ops._ptr(out), None, ops._stream(q))
+    assert st == N.STATUS_PRECONDITION
+    assert "caller-owned workspace" in N.last_error()
+
+
+def test_static_scratch_default_params_and_no_device_allocation(pp, cuda):
+    """params = NULL takes the defaults (f32 q and out, stream-K plan) and
+    matches the workspace entry point; a run of calls after the first leaves
+    the device's free memory unchanged (nothing is allocated)."""
+    ops, N = pp.int8_kv_ops, pp._native
+    g = torch.Generator(device=cuda)
+    g.manual_seed(13)
+    branches, heads, d, cap = 4, 8, 128, 900
+    rows = branches * heads
+    k, ks = ops.quantize(torch.randn(rows, cap, d, device=cuda, generator=g))
+    v, vs = ops.quantize(torch.randn(rows, cap, d, device=cuda, generator=g))
+    lens = torch.tensor([900, 3, 512, 77], dtype=torch.int32, device=cuda)
+    q = torch.randn(rows, d, device=cuda, generator=g)
+    out = torch.empty(rows, d, dtype=torch.float32, device=cuda)
+    arena = ops.arena_struct(k, v, ks, vs, heads)
+
+    def call():
+        N.check(N.lib.pp_b200_decode_attention_static(C.byref(arena), None, ops._ptr(q), None, None, ops._ptr(lens),
+                                                      ops._ptr(out), None, ops._stream(q)))
+
+    call()
+    want = ops.decode_attention(q, k, v, ks, vs, lens, heads, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), want.cpu().numpy(), rtol=1e-5, atol=2e-5)
+    free_before, _ = torch.cuda.mem_get_info(cuda)
+    for _ in range(8):
+        call()
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info(cuda)
+    assert free_after == free_before
+    np.testing.assert_allclose(out.cpu().numpy(), want.cpu().numpy(), rtol=1e-5, atol=2e-5)
