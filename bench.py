@@ -58,6 +58,17 @@ WORKLOADS = {
     "float": dict(branches=32, heads=16, d=64, ctx=4096, layers=24, kv="bf16",
                   desc="float-KV decode attention: 32 branches x 16 heads x d64, bf16 K/V, context 4096, "
                        "24 layer caches, f32 q/out (the reference's F32 query and output)"),
+    # the reference model's own regime (docs/architecture.md: 24 heads x 64, context 1024): reference
+    # mode (history of `ctx - 1` int8 tokens + the current token as f32 scratch), f32 q/out as the
+    # reference's op, 8 branches (CFG 1: one row per branch), the model's 35 layer caches
+    "deployed": dict(branches=8, heads=24, d=64, ctx=1024, layers=35, refmode=True,
+                     desc="the reference model's shape: 8 branches x 24 heads x d64, 1023 int8 history tokens + "
+                          "the current token as f32 scratch (capacity 1024), f32 q/out, 35 layer caches"),
+    # BASELINE config 0 as one call per step; 64 distinct copies of the layer are rotated so that each call
+    # reads its 2.2 MB from HBM rather than L2 (64 x 2.2 MB > 126 MB)
+    "cfg0": dict(branches=1, heads=16, d=64, ctx=1024, layers=64, refmode=True, per_step_calls=1,
+                 desc="BASELINE config 0: 1 branch x 16 heads x d64, context 1024 (1023 int8 history tokens + the "
+                      "current token as f32 scratch), f32 q/out; one call per step over 64 rotated copies"),
     # ctx: mean initial context (the CPU sample's length); lengths are drawn per branch from U[lo, hi]
     "cfg2": dict(branches=64, heads=16, d=128, ctx=4224, layers=1, lo=256, hi=8192, max_steps=256,
                  desc="BASELINE config 2: 64 branches x 16 heads x d128, initial contexts U[256, 8192], per step "
@@ -68,6 +79,13 @@ WORKLOADS = {
 def bytes_per_call(w) -> int:
     rows = w["branches"] * w["heads"]
     return rows * w["ctx"] * (2 * w["d"] + 8) + rows * w["d"] * 2 + rows * w["d"] * 2
+
+
+def bytes_per_call_refmode(w) -> int:
+    """Reference mode: ctx - 1 history tokens per row, the f32 scratch K and V,
+    f32 q and out."""
+    rows = w["branches"] * w["heads"]
+    return rows * (w["ctx"] - 1) * (2 * w["d"] + 8) + rows * w["d"] * 4 * 4
 
 
 def load_peaks() -> tuple[float, str]:
@@ -227,15 +245,21 @@ def cpu_reference(w, steps: int, warmup: int, sample_branches: int, threads: int
     ks = g.uniform(0.005, 0.03, (rows, w["ctx"])).astype(np.float32)
     vs = g.uniform(0.005, 0.03, (rows, w["ctx"])).astype(np.float32)
     q = oracle.bf16_round(g.standard_normal((rows, w["d"]), dtype=np.float32))
-    lens = np.full(sample_branches, w["ctx"], np.uint32)
-    per_call = rows * w["ctx"] * (2 * w["d"] + 8) + rows * w["d"] * 4
+    sk = sv = None
+    if w.get("refmode"):  # history of ctx - 1 tokens plus the f32 scratch token
+        q = g.standard_normal((rows, w["d"]), dtype=np.float32)
+        sk = g.standard_normal((rows, w["d"]), dtype=np.float32)
+        sv = g.standard_normal((rows, w["d"]), dtype=np.float32)
+    lens = np.full(sample_branches, w["ctx"] - (1 if w.get("refmode") else 0), np.uint32)
+    per_call = (bytes_per_call_refmode(dict(w, branches=sample_branches)) if w.get("refmode") else
+                rows * w["ctx"] * (2 * w["d"] + 8) + rows * w["d"] * 4)
     for _ in range(max(0, warmup)):
-        oracle.attention(q, k, v, ks, vs, lens, w["heads"], threads=threads)
+        oracle.attention(q, k, v, ks, vs, lens, w["heads"], sk=sk, sv=sv, threads=threads)
     times = []
     t_all = time.perf_counter()
     for _ in range(max(1, steps)):
         t0 = time.perf_counter()
-        oracle.attention(q, k, v, ks, vs, lens, w["heads"], threads=threads)
+        oracle.attention(q, k, v, ks, vs, lens, w["heads"], sk=sk, sv=sv, threads=threads)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - t_all > budget_s:
             break
@@ -327,6 +351,7 @@ def run_reference_arm(args, w) -> int:
         "data": "synthetic (seeded)",
         # the same workload description as this repository's arm (what was sampled is in cpu_baseline)
         "config": attention_config(args, w, n) if args.workload in ("cfg1", "cfg4") else
+                  refmode_config(args, w, n) if w.get("refmode") else
                   {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"],
                    "heads": w["heads"], "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"],
                    "parallelism": "replicas only (host cores)"},
@@ -531,16 +556,15 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     24 layers (RMSNorm, QKV projection, fused q/k RMSNorm + RoPE + int8 append,
     int8 decode attention over history + the new token, output projection,
     RMSNorm, gate/up projection, SwiGLU, down projection) and the final
-    RMSNorm.  Projections are cuBLAS GEMMs (this library's decode-row GEMM
-    with --gemm rows); the rest are this library's kernels.  Each step appends at the next slot, so the context grows by one
+    RMSNorm.  Projections are cuBLAS GEMMs; the rest are this library's
+    kernels.  Each step appends at the next slot, so the context grows by one
     token per step.  Branches are independent: no collective in the step."""
     D = pp.decoder
     cfg = D.DecoderConfig(layers=w["layers"], width=w["width"], heads=w["heads"], head_dim=w["d"],
                           ffn_hidden=w["ffn"], max_context=w["ctx"] + args.warmup + args.steps + 8)
     B, L0 = w["branches"], w["ctx"]
     steps = args.steps
-    model = D.SyntheticDecoder(cfg, branches=B, capacity=cfg.max_context, device=dev, seed=1234 + rank,
-                               gemm=args.gemm)
+    model = D.SyntheticDecoder(cfg, branches=B, capacity=cfg.max_context, device=dev, seed=1234 + rank)
     model.fill_history(None, seed=99 + rank)
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
@@ -636,7 +660,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
             "config": {"workload": "cfg3", "desc": w["desc"], "branches_per_gpu": B, "layers": cfg.layers,
                        "width": cfg.width, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn_hidden": cfg.ffn_hidden,
                        "context": L0, "parameters": cfg.parameters(), "cuda_graph": graph is not None,
-                       "projections": "decode-row GEMM (rows_gemm)" if model.rows_gemm else "cuBLAS",
+                       "projections": "cuBLAS (torch.matmul), outside this library's kernels",
                        "parallelism": f"branch shards x{world}, weights replicated (no collective in the step)",
                        "l2": "weights 2.5 GB + history 3.3 GB per step, larger than L2; no flush"},
             "tokens_per_s": tokens_per_s,
@@ -647,7 +671,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
             "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
             "e2e": e2e,
             # plan; per layer 2 rmsnorm, qkv_rope_append, attention, swiglu (+ 4 decode-row GEMMs); final rmsnorm
-            "gpu_launches": steps * (1 + cfg.layers * (5 + (4 if model.rows_gemm else 0)) + 1),
+            "gpu_launches": steps * (1 + cfg.layers * 5 + 1),
             "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
@@ -963,6 +987,276 @@ def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     return 0
 
 
+def refmode_inputs(w, dev, seed: int):
+    """Per-layer int8 caches (N(0,1) quantized per (token, head)), f32
+    queries and f32 scratch K/V for every layer, and the per-branch history
+    length ctx - 1 (the token at index ctx - 1 is the scratch token)."""
+    from importlib import import_module
+
+    ops = import_module("pop2-bezier_b200").int8_kv_ops
+    rows, D, cap, layers = w["branches"] * w["heads"], w["d"], w["ctx"], w["layers"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    caches = []
+    for _ in range(layers):
+        k, ks = ops.quantize(torch.randn(rows, cap, D, device=dev, generator=gen), check_finite=False)
+        v, vs = ops.quantize(torch.randn(rows, cap, D, device=dev, generator=gen), check_finite=False)
+        caches.append((k, v, ks, vs))
+    qs = torch.randn(layers, rows, D, device=dev, generator=gen)
+    sks = torch.randn(layers, rows, D, device=dev, generator=gen)
+    svs = torch.randn(layers, rows, D, device=dev, generator=gen)
+    past = torch.full((w["branches"],), cap - 1, dtype=torch.int32, device=dev)
+    return caches, qs, sks, svs, past
+
+
+def refmode_plan(w):
+    """(calls per step, layer copy of call i in step s): the deployed step is
+    one call per layer cache; cfg0 is one call per step over rotated copies."""
+    if w.get("per_step_calls"):
+        return w["per_step_calls"], (lambda s, i: s % w["layers"])
+    return w["layers"], (lambda s, i: i)
+
+
+def run_refmode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """Reference-mode attention at the reference model's own shapes (workloads
+    `deployed` and `cfg0`): per call, ctx - 1 int8 history tokens per row plus
+    the current token as f32 scratch, f32 q and out, the reference's head_dim
+    64 and 1024-token capacity (int8_kv_ops.rs:44).  A step plans once (the
+    lengths are shared by the step's calls) and runs its calls; layers after
+    the first stream their history while the previous call finishes."""
+    ops, N = pp.int8_kv_ops, pp._native
+    H, D = w["heads"], w["d"]
+    caches, qs, sks, svs, past = refmode_inputs(w, dev, 1234 + rank)
+    calls, layer_of = refmode_plan(w)
+    outs = torch.empty_like(qs)
+    arenas = [ops.arena_struct(k, v, ks, vs, H) for (k, v, ks, vs) in caches]
+    mk = lambda ready, pf: ops.attn_params(q_dtype=torch.float32, out_dtype=torch.float32, plan_ready=ready,  # noqa
+                                           prefetch_history=pf and not args.no_prefetch)
+    params, p_ready, p_pf = mk(False, False), mk(True, False), mk(True, True)
+    ws = ops.new_workspace(arenas[0], params, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    lib = N.lib
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    ws_p, st_p, past_p = P(ws), P(status), P(past)
+
+    def enqueue(s: int, sp):
+        N.check(lib.pp_b200_plan_ragged(C.byref(arenas[layer_of(s, 0)]), C.byref(params), past_p, 1, ws_p,
+                                        ws.numel(), sp))
+        for i in range(calls):
+            li = layer_of(s, i)
+            N.check(lib.pp_b200_decode_attention(C.byref(arenas[li]), C.byref(p_pf if i else p_ready), P(qs[li]),
+                                                 P(sks[li]), P(svs[li]), past_p, P(outs[li]), ws_p, ws.numel(),
+                                                 st_p, sp))
+
+    for s in range(args.warmup):
+        enqueue(s, sp)
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise SystemExit(f"device status after warm-up: {N.status_message(int(status.item()))}")
+    # a call moves a few MB in a few microseconds, less than a launch from Python costs: each step pattern is
+    # recorded once as a CUDA graph (one per rotated copy for cfg0) and replayed, so the device never waits
+    # for the host
+    graphs = capture_steps(lambda s, sp_: enqueue(s, sp_), w, dev)
+
+    def step(s: int):
+        graphs[s % len(graphs)].replay()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if pg is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for s in range(args.steps):
+            step(s)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = start.elapsed_time(end)
+    ranks = per_rank(pg, dev, ms_local, args.steps, clocks)
+    ms_step = max_over_ranks(ms_local) / args.steps
+    per_call = bytes_per_call_refmode(w)
+    call_us = ms_local / (args.steps * calls) * 1e3
+    value = world * calls * per_call / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = load_peaks()
+    achieved = per_call / (call_us * 1e-6) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        # the public Python API with every call's q and scratch K/V copied in from pinned host memory and its
+        # output read back, all inside the timed region (serial on the compute stream)
+        hq, hk, hv = (t.cpu().pin_memory() for t in (qs, sks, svs))
+        ho = torch.empty(outs.shape, dtype=outs.dtype).pin_memory()
+        dq, dk, dv = (torch.empty_like(qs[0]) for _ in range(3))
+        k0, v0, ks0, vs0 = caches[0]
+
+        def e2e_step(s: int):
+            ops.plan_ragged(k0, v0, ks0, vs0, past, H, ws, scratch=True)
+            for i in range(calls):
+                li = layer_of(s, i)
+                dq.copy_(hq[li], non_blocking=True)
+                dk.copy_(hk[li], non_blocking=True)
+                dv.copy_(hv[li], non_blocking=True)
+                k, v, ks, vs = caches[li]
+                ops.decode_attention(dq, k, v, ks, vs, past, H, scratch_k=dk, scratch_v=dv, out_dtype=torch.float32,
+                                     workspace=ws, plan_ready=True, out=outs[li])
+                ho[li].copy_(outs[li], non_blocking=True)
+
+        for s in range(max(1, args.warmup)):
+            e2e_step(s)
+        e_steps = max(1, min(args.steps, 50))
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for s in range(e_steps):
+            e2e_step(s)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(s0.elapsed_time(s1) / e_steps)
+        e2e = {"value": world * calls * per_call / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": 3 * calls * qs[0].numel() * 4, "d2h_bytes_per_step": calls * qs[0].numel() * 4,
+               "ms_per_step": e_ms, "us_per_call": e_ms * 1e3 / calls, "copies": "serial on the compute stream"}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference(w, steps=20, warmup=2, sample_branches=w["branches"], threads=os.cpu_count() or 1,
+                            budget_s=10.0)
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "us_per_call": call_us, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 KV (bf16-rounded dequant), f32 scratch token, f32 q/out, f32 accumulate",
+            "data": "synthetic (seeded)",
+            "config": refmode_config(args, w, world),
+            "tokens_per_s": world * w["branches"] / (ms_step * 1e-3) if not w.get("per_step_calls") else None,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_call,
+                         "per_launch_ms": call_us * 1e-3,
+                         "timed": "timed region / attention calls (CUDA events), the step's plan charged to its calls"},
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "e2e": e2e,
+            "gpu_launches": args.steps * (1 + calls),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def capture_steps(enqueue, w, dev) -> list:
+    """One CUDA graph per distinct step of a reference-mode workload: a single
+    graph for `deployed` (every step is the same plan + 35 calls), one per
+    rotated layer copy for cfg0.  enqueue(s, stream_pointer) issues step s."""
+    n = w["layers"] if w.get("per_step_calls") else 1
+    graphs = []
+    for s in range(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            enqueue(s, C.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+        graphs.append(g)
+    torch.cuda.synchronize()
+    return graphs
+
+
+def refmode_config(args, w, world: int) -> dict:
+    return {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"], "heads": w["heads"],
+            "head_dim": w["d"], "capacity": w["ctx"], "history": w["ctx"] - 1, "layers": w["layers"],
+            "calls_per_step": refmode_plan(w)[0], "mode": "reference (f32 scratch token)", "cuda_graph": True,
+            "parallelism": f"branch shards x{world} (no collective in the step)",
+            "l2": "the rotated layer caches together exceed L2; no flush"}
+
+
+def run_reference_kernels(args, w) -> int:
+    """The reference's own CUDA kernels (pp_i8_attention + pp_i8_merge,
+    app/src/model/int8_kv.cu, compiled from the reference sources into
+    oracle/_ref/ with its NVRTC options) on the same inputs and steps as
+    run_refmode, launched with the reference's geometry (int8_kv_ops.rs:
+    143-161: grid (rows, ceil((capacity+1)/split)), 128 threads, split 128,
+    then a 64-thread merge per row).  Partials and outputs are allocated once
+    (the reference allocates them per call)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref_runner
+
+    if not ref_runner.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/int8_kv_ref.cubin was not built "
+                          "(the reference tree was absent when build() ran)"}), flush=True)
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    caches, qs, sks, svs, past = refmode_inputs(w, dev, 1234)
+    kern = ref_runner.RefInt8Kernels()
+    rows, D, cap = w["branches"] * w["heads"], w["d"], w["ctx"]
+    split = 128
+    splits = (cap + 1 + split - 1) // split
+    partial = torch.empty(rows * splits * 66, dtype=torch.float32, device=dev)
+    outs = torch.empty_like(qs)
+    calls, layer_of = refmode_plan(w)
+
+    def enqueue(s: int, sp=None):
+        for i in range(calls):
+            li = layer_of(s, i)
+            k, v, ks, vs = caches[li]
+            kern._launch("pp_i8_attention", (rows, splits), 128, (split + 128) * 4,
+                         [qs[li], k, v, ks, vs, sks[li], svs[li], past, partial, C.c_uint32(w["heads"]),
+                          C.c_uint32(cap), C.c_uint32(split), C.c_uint32(splits)])
+            kern._launch("pp_i8_merge", (rows, 1), 64, 0, [partial, outs[li], C.c_uint32(splits)])
+
+    for s in range(args.warmup):
+        enqueue(s)
+    torch.cuda.synchronize()
+    # recorded as CUDA graphs exactly as this repository's arm is (the reference launches from Rust, where a
+    # launch costs the host less than from Python)
+    graphs = capture_steps(enqueue, w, dev)
+
+    def step(s: int):
+        graphs[s % len(graphs)].replay()
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        start.record(stream)
+        for s in range(args.steps):
+            step(s)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms_step = start.elapsed_time(end) / args.steps
+    per_call = bytes_per_call_refmode(w)
+    value = calls * per_call / (ms_step * 1e-3) / 1e9
+    line = {
+        "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+        "impl": "reference", "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "us_per_call": ms_step * 1e3 / calls,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 KV (bf16-rounded dequant), f32 scratch token, f32 q/out, f32 accumulate",
+        "data": "synthetic (seeded)", "config": refmode_config(args, w, 1), "clocks": clocks.summary(),
+        "reference_kernels": "pp_i8_attention + pp_i8_merge (app/src/model/int8_kv.cu) compiled for sm_100a with "
+                             "fmad=false, prec_div=true; launch geometry of int8_kv_ops.rs:143-161, split 128; "
+                             "each step pattern replayed as a CUDA graph",
+        "gpu_launches": args.steps * 2 * calls,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -980,8 +1274,9 @@ def main() -> int:
     ap.add_argument("--no-prefetch", action="store_true", help="never stream history before the previous kernel ends")
     ap.add_argument("--kv-dtype", choices=["bf16", "f32"], default=None,
                     help="float workload: K/V element type; encode: input element type")
-    ap.add_argument("--gemm", choices=["rows", "cublas"], default="cublas",
-                    help="cfg3: projections by cuBLAS (default) or the decode-row GEMM")
+    ap.add_argument("--ref-kernels", action="store_true",
+                    help="with --impl reference and a reference-mode workload (deployed, cfg0): time the reference's "
+                         "own CUDA kernels (oracle/_ref) on the GPU instead of its arithmetic on the host cores")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     if args.layers:
@@ -993,7 +1288,11 @@ def main() -> int:
             raise SystemExit("--head-dim does not apply to the decoder workload")
         w["d"] = args.head_dim
         w["desc"] += f" (head_dim overridden to {args.head_dim})"
+    if args.ref_kernels and (args.impl != "reference" or not w.get("refmode")):
+        raise SystemExit("--ref-kernels needs --impl reference and a reference-mode workload (deployed, cfg0)")
     if args.impl == "reference":
+        if args.ref_kernels:
+            return run_reference_kernels(args, w)
         return run_reference_arm(args, w)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1023,6 +1322,8 @@ def main() -> int:
         return run_encode(args, w, pp, pg, world, rank, local, dev)
     if args.workload == "float":
         return run_float(args, w, pp, pg, world, rank, local, dev)
+    if w.get("refmode"):
+        return run_refmode(args, w, pp, pg, world, rank, local, dev)
 
     # ---- branch shard of this rank (independent branches, no collective)
     total_branches = w["branches"] * world

@@ -340,28 +340,6 @@ int32_t pp_b200_renyi_sample(const float* raw, const float* uniforms, const uint
                              uint32_t batch, uint32_t choices, uint32_t guidance, float alpha, float cfg,
                              uint32_t token_offset, void* stream);
 
-/* Decode-row GEMM for the projections of one decode step: replaces the
- * reference's `x.matmul(&w.t())` on the batch's rows (app/src/model/
- * batch.rs:134,155-170, cuBLAS underneath).  out[i, j] = sum_k x[i, k] w[j, k]
- * in bf16 with f32 accumulation, for 1 <= m <= 16 rows of x.  The weights are
- * used in a packed layout made once by pp_b200_rows_gemm_pack (at weight-load
- * time): the kernel then streams each SM's share of them as large
- * contiguous copies.
- *   x         bf16 [m, k], row stride ldx elements (16-byte aligned rows)
- *   packed_w  n * k * 2 bytes from pp_b200_rows_gemm_pack (16-byte aligned)
- *   out       bf16 [m, n], row stride ldo elements (4-byte aligned)
- * n % 8 == 0, k % 64 == 0.  The result is deterministic.  Launched as a programmatic dependent: it streams
- * the weights before the previous kernel on the stream completes and reads x
- * only after.  status (nullable): PP_DEV_WAIT_TIMEOUT. */
-int32_t pp_b200_rows_gemm(const void* x, uint64_t ldx, const void* packed_w, void* out, uint64_t ldo, uint32_t m,
-                          uint32_t n, uint32_t k, uint32_t* status, void* stream);
-
-/* Packs w bf16 [n, k] (row stride ldw elements, 16-byte aligned rows) for
- * pp_b200_rows_gemm into `packed` (n * k * 2 bytes, 16-byte aligned): blocks of
- * 8 rows, each [k / 64][8 rows][64 elements] with the 16-byte chunks of row r
- * in order c ^ r.  n % 8 == 0, k % 64 == 0. */
-int32_t pp_b200_rows_gemm_pack(const void* w, uint64_t ldw, uint32_t n, uint32_t k, void* packed, void* stream);
-
 /* On-device self-check run before int8 caches are created: replaces
  * int8_kv_ops::prepare (int8_kv_ops.rs:57-103) and is called where
  * PrimitiveModel::prepare_int8_kv calls it (int8_policy.rs:29-56).  Runs the

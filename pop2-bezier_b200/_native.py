@@ -54,8 +54,6 @@ EXPORTED = (
     "pp_b200_float_attention_workspace_size",
     "pp_b200_plan_ragged_float",
     "pp_b200_decode_attention_float",
-    "pp_b200_rows_gemm",
-    "pp_b200_rows_gemm_pack",
     "pp_b200_prepare",
     "pp_b200_prepare_optional",
 )
@@ -160,8 +158,6 @@ def _load() -> C.CDLL:
         "pp_b200_float_attention_workspace_size": (sz, [P(PpFloatKv), P(PpAttnParams)]),
         "pp_b200_plan_ragged_float": (i32, [P(PpFloatKv), P(PpAttnParams), vp, vp, sz, vp]),
         "pp_b200_decode_attention_float": (i32, [P(PpFloatKv), P(PpAttnParams), vp, u64, vp, vp, vp, sz, vp, vp]),
-        "pp_b200_rows_gemm": (i32, [vp, u64, vp, vp, u64, u32, u32, u32, vp, vp]),
-        "pp_b200_rows_gemm_pack": (i32, [vp, u64, u32, u32, vp, vp]),
         "pp_b200_prepare": (i32, [i32]),
         "pp_b200_prepare_optional": (i32, [i32, u32, u32, i32, u32, u32]),
     }

@@ -29,7 +29,6 @@ SOURCES = [
     ("csrc/kernels/attention.cu", []),
     ("csrc/kernels/attention_static.cu", []),
     ("csrc/kernels/decoder.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
-    ("csrc/kernels/gemm.cu", []),
     ("csrc/kernels/sampling.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
     ("csrc/host/abi.cpp", []),
     ("csrc/host/sched.cpp", []),

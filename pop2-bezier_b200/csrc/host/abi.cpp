@@ -77,7 +77,6 @@ int32_t device_info(DeviceInfo& out) {
                         "CUDA_ERROR_NO_BINARY_FOR_GPU: this library is built for sm_100a (B200); device is sm_%d%d",
                         d.major, minor);
         if ((e = pp::configure_attention_kernels(dev)) != cudaSuccess) return cuda_fail(e, "kernel configuration");
-        if ((e = pp::configure_rows_gemm()) != cudaSuccess) return cuda_fail(e, "kernel configuration");
         if (!g_encode) {
             void* fn = nullptr;
             cudaDriverEntryPointQueryResult q{};
@@ -641,46 +640,6 @@ const char* pp_b200_status_message(uint32_t bits) {
     return "unknown device status";
 }
 
-
-int32_t pp_b200_rows_gemm_pack(const void* w, uint64_t ldw, uint32_t n, uint32_t k, void* packed, void* stream) {
-    if (n == 0 || n % 8 != 0 || k == 0 || k % 64 != 0)
-        return fail(PP_STATUS_PRECONDITION, "rows_gemm_pack geometry: n=%u (multiple of 8) k=%u (multiple of 64)", n, k);
-    if (!w || !packed) return fail(PP_STATUS_PRECONDITION, "rows_gemm_pack: NULL pointer");
-    if (ldw < k || ldw % 8 || !aligned(w, 16) || !aligned(packed, 16))
-        return fail(PP_STATUS_PRECONDITION, "rows_gemm_pack: w rows and packed must start on 16-byte boundaries");
-    DeviceInfo d;
-    int32_t s;
-    if ((s = device_info(d))) return s;
-    cudaError_t e = pp::launch_rows_gemm_pack(w, ldw, n, k, packed, (cudaStream_t)stream);
-    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "rows_gemm_pack launch");
-}
-
-int32_t pp_b200_rows_gemm(const void* x, uint64_t ldx, const void* packed_w, void* out, uint64_t ldo, uint32_t m,
-                          uint32_t n, uint32_t k, uint32_t* status, void* stream) {
-    if (m == 0 || m > 16 || n == 0 || n % 8 != 0 || k == 0 || k % 64 != 0 || !pp::rows_gemm_supported(k))
-        return fail(PP_STATUS_PRECONDITION,
-                    "rows_gemm geometry: m=%u (1..16) n=%u (multiple of 8) k=%u (multiple of 64)", m, n, k);
-    if (!x || !packed_w || !out) return fail(PP_STATUS_PRECONDITION, "rows_gemm: NULL pointer");
-    if (ldx < k || ldo < n || (ldx * 2) % 16 || ldo % 2 || !aligned(x, 16) || !aligned(packed_w, 16) ||
-        !aligned(out, 4) || ldx * 2 >= (1ull << 40))
-        return fail(PP_STATUS_PRECONDITION, "rows_gemm: x rows and packed w must start on 16-byte boundaries, out rows on 4");
-    DeviceInfo d;
-    int32_t s;
-    if ((s = device_info(d))) return s;
-    // 3-D map {64 k, row, k / 64}: one copy brings 16 rows x 512 k of x
-    CUtensorMap map_x;
-    cuuint64_t dims[3] = {64, m, k / 64};
-    cuuint64_t strides[2] = {ldx * 2, 128};
-    cuuint32_t box[3] = {64, 16, 8};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(&map_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(PP_STATUS_PRECONDITION, "cuTensorMapEncodeTiled (rows_gemm x) failed: %d", (int)r);
-    cudaError_t e = pp::launch_rows_gemm(map_x, packed_w, out, ldo, m, n, k, (uint32_t)d.num_sms, status,
-                                         (cudaStream_t)stream);
-    return e == cudaSuccess ? PP_STATUS_OK : cuda_fail(e, "rows_gemm launch");
-}
 
 int32_t pp_b200_diag_bounded_wait(uint32_t* status, uint32_t limit_us, void* stream) {
     if (!status || limit_us == 0 || limit_us > 1000000)

@@ -164,14 +164,6 @@ uint32_t attention_stage_tokens();
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind);
 cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t stream);
 
-// Decode-row GEMM (gemm.cu): out[m, n] = sum_k x[m, k] w[n, k], m <= 16, bf16.
-bool rows_gemm_supported(uint32_t k);
-cudaError_t configure_rows_gemm();
-cudaError_t launch_rows_gemm(const CUtensorMap& map_x, const void* packed_w, void* out, uint64_t ldo, uint32_t m,
-                             uint32_t n, uint32_t k, uint32_t num_sms, uint32_t* status, cudaStream_t stream);
-cudaError_t launch_rows_gemm_pack(const void* w, uint64_t ldw, uint32_t n, uint32_t k, void* packed,
-                                  cudaStream_t stream);
-
 // Records `msg` as the calling thread's last error and returns `status`.
 int32_t fail_msg(int32_t status, const char* msg);
 

@@ -7,8 +7,6 @@ Operations (ctypes over libpp_b200.so, torch tensors for memory):
                     (app/src/model/batch.rs:143-155, int8_cache.rs:326-359)
   swiglu            graph_ops::swiglu (graph_ops.rs:175-193)
   rmsnorm           candle_nn::ops::rms_norm with an optional residual add
-  rows_gemm         x.matmul(&w.t()) for the <= 16 rows of a decode step,
-                    streaming the weights (batch.rs:134,155-170)
   rope_parameters   the [q_norm | k_norm | cos | sin] block of the reference's
                     qk_rope_parameters, with PrimitiveModel's RoPE tables
                     (mod.rs:322-330)
@@ -18,9 +16,9 @@ SyntheticDecoder runs the batched decode step of PrimitiveModel
 QKV projection -> q/k RMSNorm + RoPE + int8 append -> int8 decode attention
 (history + the current token as f32 scratch) -> output projection + residual
 -> RMSNorm -> gate/up projection -> SwiGLU -> down projection + residual, then
-the final RMSNorm.  The projections are cuBLAS GEMMs (torch.matmul) or, with
-gemm="rows", this library's decode-row GEMM (rows_gemm); everything else is
-this library's kernels.
+the final RMSNorm.  The projections are cuBLAS GEMMs (torch.matmul), as the
+reference's are (`x.matmul(&w.t())`, batch.rs:134,155-170); everything else
+is this library's kernels.
 """
 from __future__ import annotations
 
@@ -134,34 +132,6 @@ def swiglu(x: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     return out
 
 
-def rows_gemm_pack(w: torch.Tensor) -> torch.Tensor:
-    """The packed layout of bf16 w [n, k] that rows_gemm streams (made once,
-    when the weights are loaded): a uint8 tensor of n * k * 2 bytes."""
-    ops._require_cuda(w)
-    if w.dim() != 2 or w.dtype != torch.bfloat16 or w.stride(1) != 1:
-        raise N.PreconditionError("rows_gemm_pack expects bf16 w [n, k] with unit stride along k")
-    n, k = w.shape
-    packed = torch.empty(n * k * 2, dtype=torch.uint8, device=w.device)
-    N.check(N.lib.pp_b200_rows_gemm_pack(ops._ptr(w), w.stride(0), n, k, ops._ptr(packed), ops._stream(w)))
-    return packed
-
-
-def rows_gemm(x: torch.Tensor, packed_w: torch.Tensor, n: int, *, out: torch.Tensor | None = None,
-              status: torch.Tensor | None = None) -> torch.Tensor:
-    """out = x @ w.T for bf16 x [m, k] (m <= 16, unit stride along k) and the
-    packed form of w [n, k] (rows_gemm_pack); f32 accumulation, deterministic."""
-    ops._require_cuda(x, packed_w, out)
-    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1 or packed_w.dtype != torch.uint8 \
-            or packed_w.numel() != n * x.shape[1] * 2:
-        raise N.PreconditionError("rows_gemm expects bf16 x [m, k] and w [n, k] packed by rows_gemm_pack")
-    m, k = x.shape
-    if out is None:
-        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
-    N.check(N.lib.pp_b200_rows_gemm(ops._ptr(x), x.stride(0), ops._ptr(packed_w), ops._ptr(out), out.stride(0), m, n, k,
-                                    ops._ptr(status), ops._stream(x)))
-    return out
-
-
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, *, residual: torch.Tensor | None = None,
             x_sum: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """RMSNorm over the last dim of a 2-D x; with `residual`, x + residual is
@@ -201,9 +171,12 @@ class SyntheticDecoder:
     independent branches of up to `capacity` tokens."""
 
     def __init__(self, cfg: DecoderConfig, branches: int, capacity: int, device, seed: int = 0,
-                 dtype: torch.dtype = torch.bfloat16, gemm: str = "cublas"):
+                 dtype: torch.dtype = torch.bfloat16, split_tokens: int = 0):
         self.cfg, self.branches, self.capacity = cfg, branches, capacity
         self.prefetch = True  # see PP_ATTN_PREFETCH_HISTORY
+        # 0: stream-K plan balanced over the SMs; > 0: fixed splits of that many tokens, which make every
+        # branch's result independent of the other branches in the batch
+        self.split_tokens = split_tokens
         self.device = torch.device(device)
         self.dtype = dtype
         g = torch.Generator(device=self.device)
@@ -224,8 +197,7 @@ class SyntheticDecoder:
         self.final_norm = norm(w)
         self.arenas = [kv_cache.Int8KvArena.zeros(branches, h, d, capacity, self.device) for _ in range(cfg.layers)]
         a0 = self.arenas[0].struct()
-        self._params = ops.attn_params(q_dtype=dtype, out_dtype=dtype)
-        self._params_ready = ops.attn_params(q_dtype=dtype, out_dtype=dtype, plan_ready=True)
+        self._params = ops.attn_params(q_dtype=dtype, out_dtype=dtype, split_tokens=split_tokens)
         self.workspace = ops.new_workspace(a0, self._params, self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         rows = branches * h
@@ -238,20 +210,7 @@ class SyntheticDecoder:
             att=torch.empty(rows, d, dtype=dtype, device=self.device),
             act=torch.empty(branches, f, dtype=dtype, device=self.device),
             out=torch.empty(branches, w, dtype=dtype, device=self.device),
-            qkv=torch.empty(branches, 3 * w, dtype=dtype, device=self.device),
-            proj=torch.empty(branches, w, dtype=dtype, device=self.device),
-            gate_up=torch.empty(branches, 2 * f, dtype=dtype, device=self.device),
-            down=torch.empty(branches, w, dtype=dtype, device=self.device),
         )
-        # projections: cuBLAS by default (inside a CUDA graph it matches or beats the
-        # decode-row GEMM on these shapes); gemm="rows" selects rows_gemm where its
-        # shape rules hold
-        shapes = [(3 * w, w), (w, w), (2 * f, w), (w, f)]
-        self.rows_gemm = (gemm == "rows" and branches <= 16 and dtype == torch.bfloat16
-                          and all(n % 8 == 0 and k % 64 == 0 for n, k in shapes))
-        # the decode-row GEMM streams its weights in a packed layout made once here
-        self.packed = [{name: rows_gemm_pack(L[name]) for name in ("qkv", "proj", "gate_up", "down")}
-                       for L in self.layers] if self.rows_gemm else None
 
     def fill_history(self, lengths: torch.Tensor, seed: int = 1) -> None:
         """Random int8 history (codes and scales) for every layer, as if
@@ -278,14 +237,11 @@ class SyntheticDecoder:
         (library and cuBLAS set-up happen on first use)."""
         return CapturedStep(self, past, advance)
 
-    def _linear(self, x: torch.Tensor, li: int, name: str, out: torch.Tensor) -> torch.Tensor:
-        w = self.layers[li][name]
-        if self.rows_gemm:
-            return rows_gemm(x, self.packed[li][name], w.shape[0], out=out, status=self.status)
-        return torch.matmul(x, w.t())
+    def _linear(self, x: torch.Tensor, li: int, name: str) -> torch.Tensor:
+        return torch.matmul(x, self.layers[li][name].t())
 
     def step(self, x: torch.Tensor, past: torch.Tensor, positions: torch.Tensor | None = None, *,
-             commit: bool = True, probe=None) -> torch.Tensor:
+             commit: bool = True, lengths: torch.Tensor | None = None, probe=None) -> torch.Tensor:
         """One decode token for every branch.  x [branches, width] (the input
         embedding), past u32/i32 [branches] (tokens already in each branch's
         cache; the new K/V go to slot past[b]); returns the final-normed
@@ -293,35 +249,40 @@ class SyntheticDecoder:
         commit=False is the reference's partial query (int8_cache.rs:305-310):
         slot past[b] receives the placeholder (zero codes, scale 1) and the
         attention still sees the current token through the f32 scratch.
+        lengths (default: past) is the history each branch's attention reads;
+        0 makes a branch attend to its current token only, with no history
+        traffic (a retired lane riding along in the batch).
         probe(layer, q, scratch_k, scratch_v, arena, attention_out), when
         given, is called after each layer's attention is enqueued (eager
         steps only; it may synchronise and read the tensors)."""
         cfg, b = self.cfg, self._buf
         H, d = cfg.heads, cfg.head_dim
         pos = past if positions is None else positions
+        hist = past if lengths is None else lengths
         a0 = self.arenas[0]
         # one plan per step for every layer's attention (reference mode: history + scratch token)
-        ops.plan_ragged(a0.k, a0.v, a0.k_scale, a0.v_scale, past, H, self.workspace, scratch=True)
+        ops.plan_ragged(a0.k, a0.v, a0.k_scale, a0.v_scale, hist, H, self.workspace, scratch=True,
+                        split_tokens=self.split_tokens)
         xr = x
         residual = None
         for li, (L, arena) in enumerate(zip(self.layers, self.arenas)):
             rmsnorm(xr, L["norm1"], residual=residual, x_sum=xr if residual is not None else None, out=b["normed"])
-            qkv = self._linear(b["normed"], li, "qkv", b["qkv"])
+            qkv = self._linear(b["normed"], li, "qkv")
             qkv_rope_append(qkv, L["rope"], pos, arena, past, cfg.max_context, commit=commit, q_out=b["q"],
                             scratch_k=b["sk"], scratch_v=b["sv"], status=self.status)
             # qkv_rope_append writes slot past[b], after the history: the attention may stream
             # the history while it finishes
-            ops.decode_attention(b["q"], arena.k, arena.v, arena.k_scale, arena.v_scale, past, H,
+            ops.decode_attention(b["q"], arena.k, arena.v, arena.k_scale, arena.v_scale, hist, H,
                                  scratch_k=b["sk"], scratch_v=b["sv"], out_dtype=self.dtype,
-                                 workspace=self.workspace, plan_ready=True, status=self.status, out=b["att"],
-                                 prefetch_history=self.prefetch)
+                                 split_tokens=self.split_tokens, workspace=self.workspace, plan_ready=True,
+                                 status=self.status, out=b["att"], prefetch_history=self.prefetch)
             if probe is not None:
                 probe(li, b["q"], b["sk"], b["sv"], arena, b["att"])
-            proj = self._linear(b["att"].view(self.branches, H * d), li, "proj", b["proj"])
+            proj = self._linear(b["att"].view(self.branches, H * d), li, "proj")
             rmsnorm(xr, L["norm2"], residual=proj, x_sum=xr, out=b["normed"])
-            gate_up = self._linear(b["normed"], li, "gate_up", b["gate_up"])
+            gate_up = self._linear(b["normed"], li, "gate_up")
             swiglu(gate_up, out=b["act"])
-            residual = self._linear(b["act"], li, "down", b["down"])
+            residual = self._linear(b["act"], li, "down")
         return rmsnorm(xr, self.final_norm, residual=residual, x_sum=xr, out=b["out"])
 
 

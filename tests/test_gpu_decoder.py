@@ -184,12 +184,10 @@ def _torch_step(m, x: torch.Tensor, past: torch.Tensor, k_hist, v_hist, ks_hist,
     return rms(h, m.final_norm)
 
 
-@pytest.mark.parametrize("gemm", ["cublas", "rows"])
-def test_synthetic_decoder_step_matches_torch_restatement(pp, cuda, gemm):
+def test_synthetic_decoder_step_matches_torch_restatement(pp, cuda):
     D = pp.decoder
     cfg = D.DecoderConfig(layers=3, width=512, heads=4, head_dim=128, ffn_hidden=1024, max_context=128)
-    m = D.SyntheticDecoder(cfg, branches=3, capacity=100, device=cuda, seed=5, gemm=gemm)
-    assert m.rows_gemm == (gemm == "rows")
+    m = D.SyntheticDecoder(cfg, branches=3, capacity=100, device=cuda, seed=5)
     m.fill_history(None, seed=6)
     past = torch.tensor([17, 0, 99], dtype=torch.int32, device=cuda)
     hist = [(a.k.clone(), a.v.clone(), a.k_scale.clone(), a.v_scale.clone()) for a in m.arenas]
@@ -206,13 +204,12 @@ def test_synthetic_decoder_step_matches_torch_restatement(pp, cuda, gemm):
     assert all((a.k_scale[rows, slot] != hk[2][rows, slot]).all() for a, hk in zip(m.arenas, hist))
 
 
-@pytest.mark.parametrize("gemm", ["cublas", "rows"])
-def test_captured_step_replays_the_eager_step(pp, cuda, gemm):
+def test_captured_step_replays_the_eager_step(pp, cuda):
     """The step recorded as a CUDA graph gives the eager step's bits, and its
     history length advances by one per replay."""
     D = pp.decoder
     cfg = D.DecoderConfig(layers=2, width=256, heads=2, head_dim=128, ffn_hidden=512, max_context=64)
-    m = D.SyntheticDecoder(cfg, branches=3, capacity=64, device=cuda, seed=8, gemm=gemm)
+    m = D.SyntheticDecoder(cfg, branches=3, capacity=64, device=cuda, seed=8)
     m.fill_history(None, seed=9)
     gen = torch.Generator(device=cuda).manual_seed(10)
     xs = [torch.randn(3, cfg.width, device=cuda, generator=gen).to(torch.bfloat16) for _ in range(3)]
