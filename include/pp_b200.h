@@ -275,6 +275,27 @@ int32_t pp_b200_check_write_offsets(const uint64_t* past_lens, uint64_t count, u
 int32_t pp_b200_sched_partition(const uint64_t* cost, uint32_t n_branches, uint32_t n_shards,
                                 uint32_t* shard_of_branch, uint64_t* shard_cost);
 
+/* parallel_seed (app/src/inference/batch.rs:9-11): the seed of lane `lane`
+ * of a parallel generation seeded `base` is base + lane (wrapping). */
+uint64_t pp_b200_sched_lane_seed(uint64_t base, uint64_t lane);
+
+/* Draw `draw` (from 0) of the lane stream seeded `lane_seed`: the draw-th
+ * output of a SplitMix64 generator seeded lane_seed, top 24 bits / 2^24, a
+ * float in [0, 1).  The host form of pp_b200_sched_uniforms, bit for bit.
+ * Replaces the per-lane StdRng draws of device::draw_uniforms
+ * (app/src/inference/batch.rs:747-754) with a counter-based stream, so a
+ * lane draws the same values whichever shard or batch row it occupies. */
+float pp_b200_sched_uniform(uint64_t lane_seed, uint64_t draw);
+
+/* One sampling uniform per batch row on the device: for rows with
+ * active[r] != 0, out[r] = pp_b200_sched_uniform(lane_seeds[r], draws[r]) and
+ * draws[r] += 1; inactive rows get 0 and keep their counter (a retired lane
+ * draws nothing, as the reference draws only for ready lanes).
+ * lane_seeds, draws: device u64 [rows]; active: device u32 [rows]; out:
+ * device f32 [rows]. */
+int32_t pp_b200_sched_uniforms(const uint64_t* lane_seeds, uint64_t* draws, const uint32_t* active, uint32_t rows,
+                               float* out, void* stream);
+
 /* ---- decoder step around the int8 KV path (graph_ops.cu / batch.rs) ---- */
 
 /* Geometry of a QKV projection output: rows (batch rows) x [q | k | v], each

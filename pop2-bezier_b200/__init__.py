@@ -11,6 +11,7 @@ from . import kv_cache  # noqa: F401
 from . import decoder  # noqa: F401
 from . import sampling  # noqa: F401
 from . import fused_attention  # noqa: F401
+from . import sched  # noqa: F401
 from ._native import (  # noqa: F401
     ExecutionUncertainError,
     InvalidOutputError,
@@ -18,5 +19,5 @@ from ._native import (  # noqa: F401
     abi_version,
 )
 
-__all__ = ["int8_kv_ops", "kv_cache", "decoder", "sampling", "abi_version", "PreconditionError", "InvalidOutputError",
+__all__ = ["int8_kv_ops", "kv_cache", "decoder", "sampling", "fused_attention", "sched", "abi_version", "PreconditionError", "InvalidOutputError",
            "ExecutionUncertainError"]

@@ -46,6 +46,9 @@ EXPORTED = (
     "pp_b200_checked_batch_rows",
     "pp_b200_check_write_offsets",
     "pp_b200_sched_partition",
+    "pp_b200_sched_lane_seed",
+    "pp_b200_sched_uniform",
+    "pp_b200_sched_uniforms",
     "pp_b200_qkv_rope",
     "pp_b200_qkv_rope_append",
     "pp_b200_swiglu",
@@ -150,6 +153,9 @@ def _load() -> C.CDLL:
         "pp_b200_checked_batch_rows": (i32, [u64, u32, P(u64)]),
         "pp_b200_check_write_offsets": (i32, [P(u64), u64, u32, u32, u32]),
         "pp_b200_sched_partition": (i32, [P(u64), u32, u32, P(u32), P(u64)]),
+        "pp_b200_sched_lane_seed": (u64, [u64, u64]),
+        "pp_b200_sched_uniform": (C.c_float, [u64, u64]),
+        "pp_b200_sched_uniforms": (i32, [vp, vp, vp, u32, vp, vp]),
         "pp_b200_qkv_rope": (i32, [P(PpQkvRope), vp, vp, vp, vp, vp, vp]),
         "pp_b200_qkv_rope_append": (i32, [P(PpQkvRope), vp, vp, vp, P(PpKvArena), vp, u32, vp, vp, vp, vp, vp]),
         "pp_b200_swiglu": (i32, [vp, vp, u64, u32, i32, vp]),

@@ -30,11 +30,12 @@ SOURCES = [
     ("csrc/kernels/attention_static.cu", []),
     ("csrc/kernels/decoder.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
     ("csrc/kernels/sampling.cu", ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]),
+    ("csrc/kernels/lanes.cu", []),
     ("csrc/host/abi.cpp", []),
     ("csrc/host/sched.cpp", []),
     ("csrc/host/selfcheck.cpp", []),
 ]
-HEADERS = ["csrc/kernels/common.cuh", "csrc/kernels/quant_row.cuh", "csrc/host/internal.h"]
+HEADERS = ["csrc/kernels/common.cuh", "csrc/kernels/quant_row.cuh", "csrc/kernels/lanes.cuh", "csrc/host/internal.h"]
 
 
 def nvcc() -> str:

@@ -163,6 +163,8 @@ uint32_t attention_scale_box_elems();
 uint32_t attention_stage_tokens();
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind);
 cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t stream);
+cudaError_t launch_lane_uniforms(const uint64_t* seeds, uint64_t* draws, const uint32_t* active, uint32_t rows,
+                                 float* out, cudaStream_t stream);
 
 // Records `msg` as the calling thread's last error and returns `status`.
 int32_t fail_msg(int32_t status, const char* msg);

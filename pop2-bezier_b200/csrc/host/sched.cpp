@@ -1,8 +1,10 @@
 // Host-side batch geometry, write-offset validation and the branch scheduler.
 #include <algorithm>
+#include <cstdio>
 #include <numeric>
 #include <vector>
 
+#include "../kernels/lanes.cuh"
 #include "internal.h"
 
 extern "C" {
@@ -65,6 +67,31 @@ int32_t pp_b200_sched_partition(const uint64_t* cost, uint32_t n_branches, uint3
     }
     if (shard_cost)
         for (uint32_t s = 0; s < n_shards; ++s) shard_cost[s] = load[s];
+    return PP_STATUS_OK;
+}
+
+// parallel_seed (app/src/inference/batch.rs:9-11): lane i of a parallel
+// generation seeded `base` draws from the stream seeded base + i (wrapping).
+uint64_t pp_b200_sched_lane_seed(uint64_t base, uint64_t lane) { return base + lane; }
+
+// Host restatement of the device lane streams (lanes.cuh), bit for bit.
+float pp_b200_sched_uniform(uint64_t lane_seed, uint64_t draw) { return pp::lane_uniform(lane_seed, draw); }
+
+int32_t pp_b200_sched_uniforms(const uint64_t* lane_seeds, uint64_t* draws, const uint32_t* active, uint32_t rows,
+                               float* out, void* stream) {
+    if (!lane_seeds || !draws || !active || !out || rows == 0)
+        return pp::fail_msg(PP_STATUS_PRECONDITION, "lane uniforms need seeds, draw counters, the active mask, "
+                                                    "an output and at least one row");
+    if (reinterpret_cast<uintptr_t>(lane_seeds) % 8 || reinterpret_cast<uintptr_t>(draws) % 8 ||
+        reinterpret_cast<uintptr_t>(active) % 4 || reinterpret_cast<uintptr_t>(out) % 4)
+        return pp::fail_msg(PP_STATUS_PRECONDITION, "lane uniforms: seeds and draws must be 8-byte aligned, "
+                                                    "active and out 4-byte aligned");
+    const cudaError_t e = pp::launch_lane_uniforms(lane_seeds, draws, active, rows, out, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        char msg[256];
+        snprintf(msg, sizeof msg, "EXECUTION_UNCERTAIN: lane uniforms launch failed: %s", cudaGetErrorName(e));
+        return pp::fail_msg(PP_STATUS_UNCERTAIN, msg);
+    }
     return PP_STATUS_OK;
 }
 
