@@ -69,6 +69,11 @@ WORKLOADS = {
     "cfg0": dict(branches=1, heads=16, d=64, ctx=1024, layers=64, refmode=True, per_step_calls=1,
                  desc="BASELINE config 0: 1 branch x 16 heads x d64, context 1024 (1023 int8 history tokens + the "
                       "current token as f32 scratch), f32 q/out; one call per step over 64 rotated copies"),
+    # the device sampler after the output heads (fused_sampling.rs): 16 logical rows with CFG (2 physical
+    # rows each) over a 2048-choice head, the whole head legal; 64 calls per step over rotated heads
+    "sample": dict(branches=16, heads=1, d=0, ctx=2048, layers=64, guidance=2, alpha=4.0, cfg=1.5,
+                   desc="Renyi sampling with CFG: 16 rows x 2 (CFG) x 2048 choices, alpha 4, cfg 1.5, one call "
+                        "per head, 64 heads per step"),
     # ctx: mean initial context (the CPU sample's length); lengths are drawn per branch from U[lo, hi]
     "cfg2": dict(branches=64, heads=16, d=128, ctx=4224, layers=1, lo=256, hi=8192, max_steps=256,
                  desc="BASELINE config 2: 64 branches x 16 heads x d128, initial contexts U[256, 8192], per step "
@@ -1257,6 +1262,143 @@ def run_reference_kernels(args, w) -> int:
     return 0
 
 
+def sample_inputs(w, dev, seed: int):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    B, n, calls = w["branches"], w["ctx"], w["layers"]
+    raw = torch.randn(calls, B * w["guidance"], n, device=dev, generator=g) * 3
+    uni = torch.rand(calls, B, device=dev, generator=g)
+    bounds = torch.tensor([[0, n]] * B, dtype=torch.int32, device=dev)
+    return raw, uni, bounds
+
+
+def run_sample(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
+    """The device Rényi sampler (pp_b200_renyi_sample): 64 calls per step,
+    each over its own head, recorded once as a CUDA graph and replayed (a
+    call takes microseconds, less than a launch from Python)."""
+    raw, uni, bounds = sample_inputs(w, dev, 5 + rank)
+    B, n, calls = w["branches"], w["ctx"], w["layers"]
+    out = torch.empty(calls, 3, B, dtype=torch.int32, device=dev)
+    N, ops = pp._native, pp.int8_kv_ops
+
+    def enqueue(sp):
+        for i in range(calls):
+            N.check(N.lib.pp_b200_renyi_sample(ops._ptr(raw[i]), ops._ptr(uni[i]), ops._ptr(bounds), ops._ptr(out[i]),
+                                               B, n, w["guidance"], w["alpha"], w["cfg"], 0, sp))
+
+    stream = torch.cuda.current_stream(dev)
+    enqueue(C.c_void_p(stream.cuda_stream))
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        enqueue(C.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if pg is not None:
+        pg.barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms_local = start.elapsed_time(end)
+    ranks = per_rank(pg, dev, ms_local, args.steps, clocks)
+    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    per_call = raw[0].numel() * 4 + uni[0].numel() * 4 + bounds.numel() * 4 + out[0].numel() * 4
+    us = ms_local / (args.steps * calls) * 1e3
+    peak, peak_kind = load_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200",
+            "value": world * calls * B / (ms_step * 1e-3), "unit": "sampled rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "us_per_call": us,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 logits",
+            "data": "synthetic (seeded)", "config": sample_config(args, w, world),
+            "roofline": {"bound": "latency", "achieved": per_call / (us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": per_call / (us * 1e-6) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                         "per_launch_bytes": per_call, "per_launch_ms": us * 1e-3,
+                         "timed": "64 sampler calls per step in one CUDA graph, CUDA events"},
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "e2e": None, "gpu_launches": args.steps * calls, "cpu_baseline": None}), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def sample_config(args, w, world: int) -> dict:
+    return {"workload": "sample", "desc": w["desc"], "rows_per_gpu": w["branches"], "guidance": w["guidance"],
+            "choices": w["ctx"], "alpha": w["alpha"], "cfg": w["cfg"], "calls_per_step": w["layers"],
+            "cuda_graph": True, "parallelism": f"replicas x{world}"}
+
+
+def run_reference_sampler(args, w) -> int:
+    """The reference's own pp_renyi_sample (app/src/inference/renyi_sample.cu,
+    compiled from the reference sources into oracle/_ref/) on the inputs and
+    steps of run_sample, launched as fused_sampling.rs:147-162 does (one
+    256-thread block per row, padded * 8 + 256 * 16 shared bytes) and
+    recorded in a CUDA graph the same way."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref_runner
+
+    if not os.path.exists(ref_runner.RENYI_CUBIN):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/renyi_ref.cubin was not built"}), flush=True)
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    raw, uni, bounds = sample_inputs(w, dev, 5)
+    B, n, calls = w["branches"], w["ctx"], w["layers"]
+    kern = ref_runner.RefRenyiKernel()
+    padded = 1
+    while padded < n:
+        padded <<= 1
+    out = torch.zeros(calls, 3 * B, dtype=torch.int32, device=dev)
+
+    def enqueue():
+        for i in range(calls):
+            kern._launch("pp_renyi_sample", (B, 1), 256, padded * 8 + 256 * 16,
+                         [raw[i], uni[i], bounds, out[i], C.c_uint32(B), C.c_uint32(n), C.c_uint32(w["guidance"]),
+                          C.c_float(w["alpha"]), C.c_float(w["cfg"]), C.c_uint32(0), C.c_uint32(padded)])
+
+    enqueue()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        enqueue()
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms_step = start.elapsed_time(end) / args.steps
+    print(json.dumps({
+        "metric": "decode-attn HBM GB/s (% of peak) & branch tokens/s at 1/2/4/8 B200", "impl": "reference",
+        "value": calls * B / (ms_step * 1e-3), "unit": "sampled rows/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "us_per_call": ms_step * 1e3 / calls,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 logits",
+        "data": "synthetic (seeded)", "config": sample_config(args, w, 1), "clocks": clocks.summary(),
+        "reference_kernels": "pp_renyi_sample (app/src/inference/renyi_sample.cu) compiled for sm_100a with "
+                             "fmad=false, prec_div=true; launch of fused_sampling.rs:147-162",
+        "gpu_launches": args.steps * calls,
+        "e2e": {"value": calls * B / (ms_step * 1e-3), "unit": "sampled rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1288,11 +1430,16 @@ def main() -> int:
             raise SystemExit("--head-dim does not apply to the decoder workload")
         w["d"] = args.head_dim
         w["desc"] += f" (head_dim overridden to {args.head_dim})"
-    if args.ref_kernels and (args.impl != "reference" or not w.get("refmode")):
-        raise SystemExit("--ref-kernels needs --impl reference and a reference-mode workload (deployed, cfg0)")
+    if args.ref_kernels and (args.impl != "reference" or not (w.get("refmode") or args.workload == "sample")):
+        raise SystemExit("--ref-kernels needs --impl reference and a workload the reference has kernels for "
+                         "(deployed, cfg0, sample)")
     if args.impl == "reference":
         if args.ref_kernels:
-            return run_reference_kernels(args, w)
+            return run_reference_sampler(args, w) if args.workload == "sample" else run_reference_kernels(args, w)
+        if args.workload == "sample":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference samples on the GPU only "
+                              "(fused_sampling.rs); run with --ref-kernels"}), flush=True)
+            return 0
         return run_reference_arm(args, w)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1324,6 +1471,8 @@ def main() -> int:
         return run_float(args, w, pp, pg, world, rank, local, dev)
     if w.get("refmode"):
         return run_refmode(args, w, pp, pg, world, rank, local, dev)
+    if args.workload == "sample":
+        return run_sample(args, w, pp, pg, world, rank, local, dev)
 
     # ---- branch shard of this rank (independent branches, no collective)
     total_branches = w["branches"] * world
