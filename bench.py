@@ -211,6 +211,7 @@ def attention_config(args, w, world: int) -> dict:
     """The `config` object of the cfg1 / cfg4 attention lines (both arms)."""
     return {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"], "heads": w["heads"],
             "head_dim": w["d"], "context": w["ctx"], "layers": w["layers"], "split_tokens": args.split,
+            "max_ctas": args.max_ctas,
             "parallelism": f"branch shards x{world} (no collective in the step)",
             "l2": "inputs larger than L2 (each layer cache > 126 MB), no flush"}
 
@@ -1036,7 +1037,7 @@ def run_refmode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
     outs = torch.empty_like(qs)
     arenas = [ops.arena_struct(k, v, ks, vs, H) for (k, v, ks, vs) in caches]
     mk = lambda ready, pf: ops.attn_params(q_dtype=torch.float32, out_dtype=torch.float32, plan_ready=ready,  # noqa
-                                           prefetch_history=pf and not args.no_prefetch)
+                                           prefetch_history=pf and not args.no_prefetch, max_ctas=args.max_ctas)
     params, p_ready, p_pf = mk(False, False), mk(True, False), mk(True, True)
     ws = ops.new_workspace(arenas[0], params, dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -1107,7 +1108,7 @@ def run_refmode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         k0, v0, ks0, vs0 = caches[0]
 
         def e2e_step(s: int):
-            ops.plan_ragged(k0, v0, ks0, vs0, past, H, ws, scratch=True)
+            ops.plan_ragged(k0, v0, ks0, vs0, past, H, ws, scratch=True, max_ctas=args.max_ctas)
             for i in range(calls):
                 li = layer_of(s, i)
                 dq.copy_(hq[li], non_blocking=True)
@@ -1115,7 +1116,7 @@ def run_refmode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                 dv.copy_(hv[li], non_blocking=True)
                 k, v, ks, vs = caches[li]
                 ops.decode_attention(dq, k, v, ks, vs, past, H, scratch_k=dk, scratch_v=dv, out_dtype=torch.float32,
-                                     workspace=ws, plan_ready=True, out=outs[li])
+                                     workspace=ws, plan_ready=True, out=outs[li], max_ctas=args.max_ctas)
                 ho[li].copy_(outs[li], non_blocking=True)
 
         for s in range(max(1, args.warmup)):
@@ -1183,6 +1184,7 @@ def refmode_config(args, w, world: int) -> dict:
     return {"workload": args.workload, "desc": w["desc"], "branches_per_gpu": w["branches"], "heads": w["heads"],
             "head_dim": w["d"], "capacity": w["ctx"], "history": w["ctx"] - 1, "layers": w["layers"],
             "calls_per_step": refmode_plan(w)[0], "mode": "reference (f32 scratch token)", "cuda_graph": True,
+            "max_ctas": args.max_ctas,
             "parallelism": f"branch shards x{world} (no collective in the step)",
             "l2": "the rotated layer caches together exceed L2; no flush"}
 
@@ -1410,6 +1412,9 @@ def main() -> int:
     ap.add_argument("--head-dim", type=int, choices=[64, 128], default=0,
                     help="override the head size (64: the reference model's own)")
     ap.add_argument("--split", type=int, default=0, help="fixed split size in tokens (0: automatic)")
+    ap.add_argument("--max-ctas", type=int, default=0,
+                    help="attention CTAs per call (0: one per SM); fewer leaves SMs on which the next call's "
+                         "CTAs start streaming while this call drains")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="cfg3: launch the step eagerly instead of as a CUDA graph")
@@ -1511,13 +1516,14 @@ def main() -> int:
     qs = torch.randn(layers, rows, D, device=dev, generator=gen).to(torch.bfloat16)
     outs = torch.empty(layers, rows, D, dtype=torch.bfloat16, device=dev)
     arenas = [ops.arena_struct(k, v, ks, vs, H) for (k, v, ks, vs) in caches]
-    params = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+    params = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
+                             max_ctas=args.max_ctas)
     params_ready = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
-                                   plan_ready=True)
+                                   plan_ready=True, max_ctas=args.max_ctas)
     # layers after the first follow another layer's attention, which writes neither this
     # layer's history nor the plan: they may stream history while it finishes
     params_prefetch = ops.attn_params(split_tokens=args.split, q_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
-                                      plan_ready=True, prefetch_history=not args.no_prefetch)
+                                      plan_ready=True, prefetch_history=not args.no_prefetch, max_ctas=args.max_ctas)
     ws = ops.new_workspace(arenas[0], params, dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -1596,11 +1602,11 @@ def main() -> int:
         def e2e_step():
             q_dev.copy_(q_host, non_blocking=True)
             k0, v0, ks0, vs0 = caches[0]
-            ops.plan_ragged(k0, v0, ks0, vs0, lengths, H, wsp, split_tokens=args.split)
+            ops.plan_ragged(k0, v0, ks0, vs0, lengths, H, wsp, split_tokens=args.split, max_ctas=args.max_ctas)
             for i, (k, v, ks, vs) in enumerate(caches):
                 ops.decode_attention(q_dev[i], k, v, ks, vs, lengths, H, out_dtype=torch.bfloat16,
                                      split_tokens=args.split, workspace=wsp, plan_ready=True, out=outs[i],
-                                     prefetch_history=i > 0 and not args.no_prefetch)
+                                     prefetch_history=i > 0 and not args.no_prefetch, max_ctas=args.max_ctas)
             o_host.copy_(outs, non_blocking=True)
 
         for _ in range(max(1, args.warmup)):
@@ -1630,11 +1636,11 @@ def main() -> int:
 
         def run(s, j):
             k0, v0, ks0, vs0 = caches[0]
-            ops.plan_ragged(k0, v0, ks0, vs0, lengths, H, wsp, split_tokens=args.split)
+            ops.plan_ragged(k0, v0, ks0, vs0, lengths, H, wsp, split_tokens=args.split, max_ctas=args.max_ctas)
             for i, (k, v, ks, vs) in enumerate(caches):
                 ops.decode_attention(q2[j][i], k, v, ks, vs, lengths, H, out_dtype=torch.bfloat16,
                                      split_tokens=args.split, workspace=wsp, plan_ready=True, out=o2[j][i],
-                                     prefetch_history=i > 0 and not args.no_prefetch)
+                                     prefetch_history=i > 0 and not args.no_prefetch, max_ctas=args.max_ctas)
 
         def down(s, j):
             o_host.copy_(o2[j], non_blocking=True)

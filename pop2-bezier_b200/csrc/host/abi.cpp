@@ -425,8 +425,8 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     L.q = q;
     L.out = out;
     L.status = status;
-    const uint32_t stage = pp::attention_stage_tokens();  // rows of one whole-stage box
-    for (int i = 0; i < 4; ++i) {
+    const uint32_t stage = pp::attention_stage_tokens(arena->head_dim);  // rows of one whole-stage box
+    for (int i = 0; i < pp::kTailBoxes; ++i) {
         if ((s = encode_codes_map(&L.tails.k[i], arena->k, *arena, 16u << i))) return s;
         if ((s = encode_codes_map(&L.tails.v[i], arena->v, *arena, 16u << i))) return s;
     }
@@ -487,7 +487,7 @@ int32_t pp_b200_decode_attention_float(const PpFloatKv* kv, const PpAttnParams* 
     L.out = out;
     L.status = status;
     const uint32_t stage = pp::attention_float_stage_tokens(kv->head_dim, L.kv_kind);
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < pp::kTailBoxes; ++i) {
         if ((s = encode_float_map(&L.tails.k[i], kv->k, kv->k_row_stride, *kv, 16u << i))) return s;
         if ((s = encode_float_map(&L.tails.v[i], kv->v, kv->v_row_stride, *kv, 16u << i))) return s;
     }

@@ -88,10 +88,11 @@ inline WsLayout ws_layout(uint32_t rows, uint32_t capacity, uint32_t head_dim, u
 // Element type of the attended K/V (internal codes, not PP_DTYPE_*).
 constexpr int kKvInt8 = 0, kKvBf16 = 1, kKvF32 = 2;
 
-// Tensor maps for segment tails: the same K / V boxes of 16, 32, 64 and 128
-// tokens, so that a tail of n tokens takes at most 4 copies per tensor.
+// Tensor maps for segment tails: the same K / V boxes of 16, 32, 64, 128 and
+// 256 tokens, so that a tail of n tokens takes at most 5 copies per tensor.
+constexpr int kTailBoxes = 5;
 struct TailMaps {
-    CUtensorMap k[4], v[4];
+    CUtensorMap k[kTailBoxes], v[kTailBoxes];
 };
 
 struct AttnLaunch {
@@ -160,7 +161,7 @@ cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t launch_combine(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t configure_attention_kernels(int device);
 uint32_t attention_scale_box_elems();
-uint32_t attention_stage_tokens();
+uint32_t attention_stage_tokens(uint32_t head_dim);
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind);
 cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t stream);
 cudaError_t launch_lane_uniforms(const uint64_t* seeds, uint64_t* draws, const uint32_t* active, uint32_t rows,

@@ -305,8 +305,11 @@ struct RegPartial {
 #ifndef PP_ATTN_NC
 #define PP_ATTN_NC 15
 #endif
-#ifndef PP_ATTN_NB
-#define PP_ATTN_NB 1
+#ifndef PP_ATTN_NB_D128
+#define PP_ATTN_NB_D128 1
+#endif
+#ifndef PP_ATTN_NB_D64
+#define PP_ATTN_NB_D64 1
 #endif
 #ifndef PP_ATTN_STAGES_D128
 #define PP_ATTN_STAGES_D128 3
@@ -334,7 +337,8 @@ struct Cfg {
     static constexpr int NC = ROW <= 128 ? PP_ATTN_NC : ROW == 256 ? 8 : 4;
     static constexpr int THREADS = (NC + 1) * 32;   // + one producer warp
     static constexpr int BOX = 16;                  // tokens per MMA block and per tail TMA box
-    static constexpr int NB = PP_ATTN_NB;           // MMA blocks per consumer warp per stage
+    // MMA blocks per consumer warp per stage (independent blocks interleaved for ILP)
+    static constexpr int NB = !SCALED ? 1 : D == 128 ? PP_ATTN_NB_D128 : PP_ATTN_NB_D64;
     static constexpr int TPW = BOX * NB;            // tokens per consumer warp per stage
     static constexpr int T = TPW * NC;              // tokens per stage
     static constexpr int KV_BYTES = T * ROW;
@@ -374,12 +378,12 @@ struct Cfg {
     // Tensor-copy destinations in shared memory must be 128-byte aligned, and
     // the swizzled tiles 1024-byte aligned (stage bases are 1024-aligned).
     static_assert((SC_BOX * 4) % 128 == 0 && OFF_KS % 128 == 0 && OFF_VS % 128 == 0, "scale boxes 128B-aligned");
-    static_assert(!SCALED || SC_BOXES == 1, "one scale box per tensor per stage");
+    static_assert(!SCALED || SC_BOXES <= 2, "at most two scale boxes per tensor per stage");
     static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && (BOX * PANEL) % 1024 == 0 &&
                       (STAGE_BOX * PANEL) % 1024 == 0 && (T * PANEL) % 1024 == 0,
                   "tiles 1024B-aligned");
     static_assert(STAGE_BYTES % 1024 == 0 && OFF_Q % 16 == 0 && OFF_META % 16 == 0, "stage layout alignment");
-    static_assert(T / BOX < 16, "a tail of fewer than T tokens is at most 15 units: one box each of 128/64/32/16");
+    static_assert(T / BOX < 32, "a tail of fewer than T tokens is at most 31 units: one box each of 256/128/64/32/16");
     static constexpr int NI = D / 16;  // q.k MMAs per 16-token block (k = 16 channels each)
     static constexpr int NJ = D / 16;  // p.V MMAs per 16-token block (m = 16 channels each)
 
@@ -508,7 +512,7 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
         fence_mbar_init();
     }
     if (warp == C::NC && lane == 0) {
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < kTailBoxes; ++i) {
             tma_prefetch_desc(&tails.k[i]);
             tma_prefetch_desc(&tails.v[i]);
         }
@@ -628,10 +632,10 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                             tma_load_3d(st + C::OFF_V + p * C::T * 128, &map_v_stage, &full[slot], p * PX, (int32_t)t,
                                         (int32_t)sd.row);
                         }
-                    } else {  // segment tail: nbox 16-token units as boxes of 128 / 64 / 32 / 16 tokens
+                    } else {  // segment tail: nbox 16-token units as boxes of 256 / 128 / 64 / 32 / 16 tokens
                         uint32_t off = 0;
 #pragma unroll
-                        for (int i = 3; i >= 0; --i) {
+                        for (int i = 4; i >= 0; --i) {
                             if (!(nbox & (1u << i))) continue;
 #pragma unroll
                             for (int p = 0; p < C::PANELS; ++p) {
@@ -651,10 +655,10 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                         tma_load_2d(st + C::OFF_V + b * C::STAGE_BOX * D, &map_v_stage, &full[slot], 0,
                                     (int32_t)(tok + b * C::STAGE_BOX));
                     }
-                } else {  // segment tail: nbox 16-token units as boxes of 128 / 64 / 32 / 16 tokens
+                } else {  // segment tail: nbox 16-token units as boxes of 256 / 128 / 64 / 32 / 16 tokens
                     uint32_t off = 0;
 #pragma unroll
-                    for (int i = 3; i >= 0; --i) {
+                    for (int i = 4; i >= 0; --i) {
                         if (!(nbox & (1u << i))) continue;
                         tma_load_2d(st + C::OFF_K + off * D, &tails.k[i], &full[slot], 0, (int32_t)(tok + off));
                         tma_load_2d(st + C::OFF_V + off * D, &tails.v[i], &full[slot], 0, (int32_t)(tok + off));
@@ -1324,7 +1328,7 @@ cudaError_t configure_attention_kernels(int /*device*/) {
 }
 
 uint32_t attention_scale_box_elems() { return Cfg<128>::SC_BOX; }
-uint32_t attention_stage_tokens() { return Cfg<128>::STAGE_BOX; }
+uint32_t attention_stage_tokens(uint32_t head_dim) { return head_dim == 128 ? Cfg<128>::STAGE_BOX : Cfg<64>::STAGE_BOX; }
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind) {
     if (kv_kind == kKvBf16) return head_dim == 128 ? Cfg<128, Kv::BF16>::T : Cfg<64, Kv::BF16>::T;
     return head_dim == 128 ? Cfg<128, Kv::F32>::T : Cfg<64, Kv::F32>::T;

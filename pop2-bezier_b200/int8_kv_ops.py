@@ -150,7 +150,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torc
                      scratch_v: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                      split_tokens: int = 0, softmax_scale: float = 0.0, workspace: torch.Tensor | None = None,
                      plan_ready: bool = False, status: torch.Tensor | None = None,
-                     out: torch.Tensor | None = None, prefetch_history: bool = False) -> torch.Tensor:
+                     out: torch.Tensor | None = None, prefetch_history: bool = False,
+                     max_ctas: int = 0) -> torch.Tensor:
     """General entry: int8 decode attention over a [rows, capacity, d] arena.
 
     q [rows, d] (or [rows, 1, d]) F32/BF16; lengths int32/uint32 [rows/heads].
@@ -179,7 +180,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torc
     odt = out_dtype or q.dtype
     arena = arena_struct(k, v, ks, vs, heads)
     params = attn_params(split_tokens=split_tokens, q_dtype=q.dtype, out_dtype=odt, softmax_scale=softmax_scale,
-                         plan_ready=plan_ready, prefetch_history=prefetch_history)
+                         plan_ready=plan_ready, prefetch_history=prefetch_history, max_ctas=max_ctas)
     if workspace is None:
         workspace = new_workspace(arena, params, q.device)
     if out is None:
@@ -191,15 +192,17 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ks: torc
 
 
 def plan_ragged(k: torch.Tensor, v: torch.Tensor, ks: torch.Tensor, vs: torch.Tensor, lengths: torch.Tensor,
-                heads: int, workspace: torch.Tensor, *, split_tokens: int = 0, scratch: bool = False) -> None:
+                heads: int, workspace: torch.Tensor, *, split_tokens: int = 0, scratch: bool = False,
+                max_ctas: int = 0) -> None:
     """Writes the attention plan for `lengths` into `workspace`, so that the
     decode_attention calls of a step that share these lengths (one per layer)
     can pass plan_ready=True with the same workspace and skip re-planning
     (the reuse DecodeMetadataCache does, decode_metadata.rs:39-142).
-    `scratch` marks reference-mode calls (a scratch token after the history)."""
+    `scratch` marks reference-mode calls (a scratch token after the history);
+    split_tokens and max_ctas must be those of the calls that reuse the plan."""
     _require_cuda(k, lengths, workspace)
     arena = arena_struct(k, v, ks, vs, heads)
-    params = attn_params(split_tokens=split_tokens)
+    params = attn_params(split_tokens=split_tokens, max_ctas=max_ctas)
     N.check(N.lib.pp_b200_plan_ragged(C.byref(arena), C.byref(params), _ptr(lengths), 1 if scratch else 0,
                                       _ptr(workspace), workspace.numel(), _stream(lengths)))
 
