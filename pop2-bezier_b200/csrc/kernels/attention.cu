@@ -309,13 +309,13 @@ struct RegPartial {
 #define PP_ATTN_NB_D128 1
 #endif
 #ifndef PP_ATTN_NB_D64
-#define PP_ATTN_NB_D64 1
+#define PP_ATTN_NB_D64 2  // two 16-token blocks per warp keep more independent work in flight
 #endif
 #ifndef PP_ATTN_STAGES_D128
 #define PP_ATTN_STAGES_D128 3
 #endif
 #ifndef PP_ATTN_STAGES_D64
-#define PP_ATTN_STAGES_D64 4
+#define PP_ATTN_STAGES_D64 3  // 480-token stages of 64 KB: three fit
 #endif
 
 // Element type of the K/V history: int8 codes with per-token scales (the
