@@ -220,39 +220,70 @@ __device__ __forceinline__ void st_out<__nv_bfloat16>(__nv_bfloat16* p, uint64_t
 }
 
 
+// The scratch token of reference-mode row r: its score q.sk (softmax scale,
+// log2 units; every lane holds it) and sv for lane l's channels [l*E, l*E+E),
+// E = D/32.  Loaded ahead of the merge that needs them, so that their latency
+// overlaps other work.
+template <int D>
+struct ScratchVals {
+    bool on;
+    float ms;
+    float sv[D / 32];
+};
+
+template <int D, typename QT>
+__device__ __forceinline__ ScratchVals<D> load_scratch(int lane, uint32_t r, const void* q, const float* sk,
+                                                       const float* sv, float scale_log2) {
+    constexpr int E = D / 32;
+    ScratchVals<D> v;
+    v.on = sk != nullptr;
+    v.ms = -INFINITY;
+    if (v.on) {
+        const QT* qr = reinterpret_cast<const QT*>(q) + (uint64_t)r * D;
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            v.sv[e] = sv[(uint64_t)r * D + lane * E + e];
+            dot += (ldq<QT>(qr, lane * E + e) * scale_log2) * sk[(uint64_t)r * D + lane * E + e];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        v.ms = dot;
+    }
+    return v;
+}
+
+// Writes row r: acc / z, or NaN for an invalid row or one whose weights sum to zero.
+template <int D, typename OT>
+__device__ __forceinline__ void store_row(int lane, uint32_t r, bool invalid, const float* acc, float z, void* out_base) {
+    constexpr int E = D / 32;
+    OT* out = reinterpret_cast<OT*>(out_base) + (uint64_t)r * D;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        st_out<OT>(out, lane * E + e, !invalid && z > 0.f ? acc[e] / z : __uint_as_float(0x7fc00000u));
+}
+
 // Log-sum-exp finish of row r by one warp (lane l owns channels [l*E, l*E+E),
-// E = D/32): merges the row's n partials (m in log2 units, z, acc), fetched in
+// E = D/32): merges the row's n partials (m in log2 units, z, acc), taken in
 // segment order from `part`, and in reference mode the f32 scratch token
 // (q.sk, sv), then writes acc / z.  The merge of pp_i8_merge
 // (int8_kv.cu:53-59) with the scratch token of pp_i8_attention (:36-37, 49)
 // folded in; an invalid row, or one whose weights sum to zero, is NaN.
-template <int D, typename QT, typename OT, typename Part>
+template <int D, typename OT, typename Part>
 __device__ __forceinline__ void finish_row(int lane, uint32_t r, uint32_t n, bool invalid, const Part& part,
-                                           const void* q, const float* sk, const float* sv, float scale_log2,
-                                           void* out_base) {
+                                           const ScratchVals<D>& sc, void* out_base) {
     constexpr int E = D / 32;
-    OT* out = reinterpret_cast<OT*>(out_base) + (uint64_t)r * D;
-    if (invalid) {
+    float acc[E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, __uint_as_float(0x7fc00000u));
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    if (invalid) {
+        store_row<D, OT>(lane, r, true, acc, 0.f, out_base);
         return;
     }
     float mx = -INFINITY;
     for (uint32_t s = 0; s < n; ++s) mx = fmaxf(mx, part.m(s));
-    float ms = -INFINITY;
-    if (sk) {
-        const QT* qr = reinterpret_cast<const QT*>(q) + (uint64_t)r * D;
-        float dot = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) dot += (ldq<QT>(qr, lane * E + e) * scale_log2) * sk[(uint64_t)r * D + lane * E + e];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        ms = dot;
-        mx = fmaxf(mx, ms);
-    }
-    float acc[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    const float ms = sc.ms;
+    if (sc.on) mx = fmaxf(mx, ms);
     float z = 0.f;
     for (uint32_t s = 0; s < n; ++s) {
         const float m = part.m(s);
@@ -261,14 +292,75 @@ __device__ __forceinline__ void finish_row(int lane, uint32_t r, uint32_t n, boo
 #pragma unroll
         for (int e = 0; e < E; ++e) acc[e] += part.acc(s, lane, e) * f;
     }
-    if (sk) {
+    if (sc.on) {
         const float f = fast_exp2(ms - mx);
         z += f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] += sv[(uint64_t)r * D + lane * E + e] * f;
+        for (int e = 0; e < E; ++e) acc[e] += sc.sv[e] * f;
     }
+    store_row<D, OT>(lane, r, false, acc, z, out_base);
+}
+
+// The final merge of a row split over n <= batch_segs<D>() segments, by the CTA
+// that completed the row last: its own partial (segment `own` of the row)
+// comes from registers and the others are all loaded at once, then the same
+// arithmetic as finish_row, in the same segment order.
+template <int D>
+__host__ __device__ constexpr uint32_t batch_segs() { return D == 128 ? 2u : 3u; }  // register budget of the batch
+
+template <int D, typename OT, typename Own>
+__device__ __forceinline__ void finish_split(int lane, uint32_t r, uint32_t n, uint32_t own, const Own& mine,
+                                             const float* base, const ScratchVals<D>& sc, void* out_base) {
+    constexpr int E = D / 32;
+    constexpr uint32_t kBatchSegs = batch_segs<D>();
+    float mv[kBatchSegs], zv[kBatchSegs], av[kBatchSegs][E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) st_out<OT>(out, lane * E + e, z > 0.f ? acc[e] / z : __uint_as_float(0x7fc00000u));
+    for (uint32_t s = 0; s < kBatchSegs; ++s) {
+        mv[s] = -INFINITY;
+        zv[s] = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) av[s][e] = 0.f;
+        if (s < n) {
+            if (s == own) {
+                mv[s] = mine.mv;
+                zv[s] = mine.zv;
+#pragma unroll
+                for (int e = 0; e < E; ++e) av[s][e] = mine.a[e];
+            } else {
+                const float* p = base + (uint64_t)s * (D + 4);  // written by other CTAs: read through L2
+                mv[s] = __ldcg(p + D);
+                zv[s] = __ldcg(p + D + 1);
+#pragma unroll
+                for (int e = 0; e < E; ++e) av[s][e] = __ldcg(p + lane * E + e);
+            }
+        }
+    }
+    float acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    float mx = -INFINITY;
+#pragma unroll
+    for (uint32_t s = 0; s < kBatchSegs; ++s)
+        if (s < n) mx = fmaxf(mx, mv[s]);
+    const float ms = sc.ms;
+    if (sc.on) mx = fmaxf(mx, ms);
+    float z = 0.f;
+#pragma unroll
+    for (uint32_t s = 0; s < kBatchSegs; ++s) {
+        if (s < n) {
+            const float f = mv[s] == -INFINITY ? 0.f : fast_exp2(mv[s] - mx);
+            z += zv[s] * f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[e] += av[s][e] * f;
+        }
+    }
+    if (sc.on) {
+        const float f = fast_exp2(ms - mx);
+        z += f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += sc.sv[e] * f;
+    }
+    store_row<D, OT>(lane, r, false, acc, z, out_base);
 }
 
 // Partials of one row in the workspace, [segment][D + 4] from `base`.
@@ -714,12 +806,15 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
     uint32_t* row_cnt = reinterpret_cast<uint32_t*>(args.ws + args.l.row_cnt);
     const uint32_t* row_seg = reinterpret_cast<const uint32_t*>(args.ws + args.l.row_seg);
     // writes output row r from its n partials (stream-K plans only)
-    auto finish_out = [&](uint32_t r, uint32_t n, const auto& part) {
+    auto finish_out = [&](uint32_t r, uint32_t n, const auto& part, const ScratchVals<D>& sc) {
         const bool invalid = n == 0 && __ldg(reinterpret_cast<const uint32_t*>(args.ws + args.l.row_len) + r) == kInvalidRow;
         if (args.out_bf16)
-            finish_row<D, QT, __nv_bfloat16>(lane, r, n, invalid, part, args.q, args.sk, args.sv, args.scale_log2, args.out);
+            finish_row<D, __nv_bfloat16>(lane, r, n, invalid, part, sc, args.out);
         else
-            finish_row<D, QT, float>(lane, r, n, invalid, part, args.q, args.sk, args.sv, args.scale_log2, args.out);
+            finish_row<D, float>(lane, r, n, invalid, part, sc, args.out);
+    };
+    auto scratch_of = [&](uint32_t r) {
+        return load_scratch<D, QT>(lane, r, args.q, args.sk, args.sv, args.scale_log2);
     };
 
     {
@@ -755,7 +850,7 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
             // invalid rows (NaN) or, in reference mode, the scratch token alone
             const uint32_t* orphans = reinterpret_cast<const uint32_t*>(args.ws + args.l.orphans);
             for (uint32_t k = blockIdx.x * C::NC + warp; k < n_orphans; k += gridDim.x * C::NC)
-                finish_out(orphans[k], 0u, GlobalPartials<D, false>{partials});
+                finish_out(orphans[k], 0u, GlobalPartials<D, false>{partials}, scratch_of(orphans[k]));
         }
     }
 
@@ -1128,6 +1223,17 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_bar[par]);
             if (warp == (int)(seg_count % C::NC)) {
+                // what the row's finish reads from global memory goes out now, before the
+                // wait for the other warps' states and the merge: the scratch token and
+                // the row's first partial
+                const uint32_t row = m0.x, row_segs = m1.w;
+                ScratchVals<D> sc;
+                sc.on = false;
+                uint32_t first_seg = 0;
+                if (args.finish) {
+                    sc = scratch_of(row);
+                    if (row_segs > 1) first_seg = __ldg(row_seg + row);
+                }
                 if (!mbar_wait_bounded(&red_bar[par], use & 1u, abort_flag, kWaitLimitNs)) {
                     *abort_flag = 1;
                     if (lane == 0 && args.status) atomicOr(args.status, PP_DEV_WAIT_TIMEOUT);
@@ -1154,9 +1260,8 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                 seg.zv = sz;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&red_free[par]);
-                const uint32_t row = m0.x, row_segs = m1.w;
                 if (args.finish && row_segs == 1) {
-                    finish_out(row, 1u, seg);
+                    finish_out(row, 1u, seg, sc);
                 } else {
                     float* dst = partials + (uint64_t)seg_slot * (D + 4);
 #pragma unroll
@@ -1175,8 +1280,16 @@ __global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
                         done = __shfl_sync(0xffffffffu, done, 0);
                         if (done == row_segs) {
                             __threadfence();
-                            finish_out(row, row_segs,
-                                       GlobalPartials<D, true>{partials + (uint64_t)__ldg(row_seg + row) * (D + 4)});
+                            const float* rp = partials + (uint64_t)first_seg * (D + 4);
+                            if (row_segs <= batch_segs<D>()) {
+                                if (args.out_bf16)
+                                    finish_split<D, __nv_bfloat16>(lane, row, row_segs, seg_slot - first_seg, seg, rp, sc,
+                                                                   args.out);
+                                else
+                                    finish_split<D, float>(lane, row, row_segs, seg_slot - first_seg, seg, rp, sc, args.out);
+                            } else {
+                                finish_out(row, row_segs, GlobalPartials<D, true>{rp}, sc);
+                            }
                             if (lane == 0) row_cnt[row] = 0u;  // zero again for the next call
                         }
                     }
@@ -1212,9 +1325,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
     const uint32_t* row_seg = reinterpret_cast<const uint32_t*>(a.ws + a.l.row_seg);
     const float* partials = reinterpret_cast<const float*>(a.ws + a.l.partials);
     const uint32_t s0 = row_seg[r], s1 = row_seg[r + 1];
-    finish_row<D, QT, OT>(lane, r, s1 - s0, row_len[r] == kInvalidRow,
-                          GlobalPartials<D, false>{partials + (uint64_t)s0 * (D + 4)}, a.q, a.sk, a.sv, a.scale_log2,
-                          a.out);
+    finish_row<D, OT>(lane, r, s1 - s0, row_len[r] == kInvalidRow,
+                      GlobalPartials<D, false>{partials + (uint64_t)s0 * (D + 4)},
+                      load_scratch<D, QT>(lane, r, a.q, a.sk, a.sv, a.scale_log2), a.out);
 }
 
 template <int D, typename QT, Kv KV>
