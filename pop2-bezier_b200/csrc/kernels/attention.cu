@@ -33,6 +33,12 @@
 namespace pp {
 namespace {
 
+// Fewest history tokens per CTA in a stream-K plan: a smaller call uses fewer
+// CTAs (a CTA's fixed cost outweighs a few hundred tokens of work).
+#ifndef PP_PLAN_MIN_TOKENS
+#define PP_PLAN_MIN_TOKENS 512
+#endif
+
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: generous, never hit in normal runs
 constexpr float kSlack = 8.0f;  // log2-domain headroom before the softmax reference point moves
 
@@ -69,6 +75,9 @@ struct PlanArgs {
     unsigned char* ws;
     WsLayout l;
     uint32_t rows, heads, capacity, split, scratch, max_ctas, min_tokens;
+    // whole rows per CTA instead of stream-K cuts when the rows are of one length and
+    // that adds fewer tokens per CTA than this (the cost of a row split across CTAs)
+    uint32_t whole_row_slack;
     uint32_t* status;
 };
 
@@ -78,7 +87,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     // trigger), so nothing can read a half-written plan.
     pdl_wait_primary();
     __shared__ uint32_t warp_tot[32];
-    __shared__ uint32_t s_n_ctas, s_per_cta, s_total, s_bad;
+    __shared__ uint32_t s_n_ctas, s_per_cta, s_total, s_bad, s_hmin, s_hmax, s_rows;
     PlanHeader* hdr = reinterpret_cast<PlanHeader*>(a.ws);
     uint32_t* row_len = reinterpret_cast<uint32_t*>(a.ws + a.l.row_len);
     uint32_t* row_seg = reinterpret_cast<uint32_t*>(a.ws + a.l.row_seg);
@@ -86,7 +95,12 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     SegDesc* segs = reinterpret_cast<SegDesc*>(a.ws + a.l.segs);
     uint32_t* row_cnt = reinterpret_cast<uint32_t*>(a.ws + a.l.row_cnt);
     uint32_t* orphans = reinterpret_cast<uint32_t*>(a.ws + a.l.orphans);
-    if (threadIdx.x == 0) s_bad = 0;
+    if (threadIdx.x == 0) {
+        s_bad = 0;
+        s_hmin = 0xffffffffu;
+        s_hmax = 0;
+        s_rows = 0;
+    }
     __syncthreads();
 
     auto history = [&](uint32_t r, bool& valid) -> uint32_t {
@@ -104,6 +118,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
         if (r < a.rows) {
             row_len[r] = valid ? h : kInvalidRow;
             if (!valid) s_bad = 1;
+            if (h) {  // rows with history: their count and length range
+                atomicMin(&s_hmin, h);
+                atomicMax(&s_hmax, h);
+                atomicAdd(&s_rows, 1u);
+            }
         }
         uint32_t tot;
         block_exclusive_scan(h, warp_tot, tot);
@@ -119,6 +138,15 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
                 uint32_t want = (total + a.min_tokens - 1) / a.min_tokens;
                 n_ctas = want < a.max_ctas ? want : a.max_ctas;
                 per = (total + n_ctas - 1) / n_ctas;
+                if (s_hmin == s_hmax) {
+                    // rows of one length h: k whole rows per CTA put every cut on a row
+                    // boundary, so no row is split across CTAs; taken when the larger
+                    // share costs less than the splits it avoids
+                    const uint32_t k = (s_rows + a.max_ctas - 1) / a.max_ctas;
+                    const unsigned long long whole = (unsigned long long)k * s_hmax;
+                    if (whole >= per && whole - per < a.whole_row_slack && whole <= 0xffffffffull)
+                        per = (uint32_t)whole;
+                }
                 n_ctas = (total + per - 1) / per;  // every CTA range non-empty
             }
         }
@@ -1458,7 +1486,10 @@ cudaError_t launch_plan(const AttnLaunch& L, cudaStream_t stream) {
     a.split = L.split;
     a.scratch = L.scratch_k ? 1u : 0u;
     a.max_ctas = L.max_ctas;
-    a.min_tokens = 32;
+    a.min_tokens = PP_PLAN_MIN_TOKENS;
+    // a split row costs its CTAs a partial merge and the row a final merge: measured worth about
+    // 1024 int8 tokens of head_dim 64 and fewer than 553 of the wider rows
+    a.whole_row_slack = (L.kv_kind == kKvInt8 && L.arena.head_dim == 64) ? 1024u : 512u;
     a.status = L.status;
     return launch_pdl(plan_kernel, dim3(1), dim3(1024), stream, a);
 }
