@@ -216,6 +216,19 @@ def attention_config(args, w, world: int) -> dict:
             "l2": "inputs larger than L2 (each layer cache > 126 MB), no flush"}
 
 
+_DATA_GROUP = None
+
+
+def data_group(pg):
+    """The NCCL group of all ranks that carries the outputs' final gather over
+    NVLink, created at its first use, after every timed region (the default
+    group is gloo: barriers and timing reductions on host tensors)."""
+    global _DATA_GROUP
+    if _DATA_GROUP is None:
+        _DATA_GROUP = pg.new_group(backend="nccl")
+    return _DATA_GROUP
+
+
 def per_rank(pg, dev, ms_local: float, steps: int, clocks: "ClockSampler") -> list:
     """Every rank's own device time per step and its median SM clock during
     the timed region, gathered to every rank (one all_gather, outside the
@@ -223,7 +236,7 @@ def per_rank(pg, dev, ms_local: float, steps: int, clocks: "ClockSampler") -> li
     power budget) from a rank that did more work or waited on its host."""
     c = clocks.summary()
     mine = torch.tensor([ms_local / max(1, steps), float(c["sm_mhz"] or 0.0), float(clocks.reasons)],
-                        dtype=torch.float64, device=dev)
+                        dtype=torch.float64)
     if pg is None:
         rows = [mine]
     else:
@@ -434,7 +447,7 @@ def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        t = torch.tensor([x], dtype=torch.float64)
         if pg is not None:
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
@@ -518,7 +531,7 @@ def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                "serial_value": world * per_step / (serial_ms * 1e-3) / 1e9, "serial_ms_per_step": serial_ms}
 
     if pg is not None:
-        shards.gather(pg, outs[steps - 1].view(B, H, D).contiguous())
+        shards.gather(pg, outs[steps - 1].view(B, H, D).contiguous(), group=data_group(pg))
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -541,7 +554,7 @@ def run_cfg2(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_step,
                          "per_launch_ms": ms_local / steps,
                          "timed": "timed region / steps: append + plan + attention per step (CUDA events)"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None,
             "e2e": e2e,
             "gpu_launches": steps * (4 if args.split else 3),  # append, plan, attention (+ combine)
             "cpu_baseline": cpu,
@@ -604,7 +617,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        t = torch.tensor([x], dtype=torch.float64)
         if pg is not None:
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
@@ -655,7 +668,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
 
     if pg is not None:
         shards = pp.kv_cache.BranchShards([L0] * (B * world), world, rank)
-        shards.gather(pg, outs[-1].contiguous())
+        shards.gather(pg, outs[-1].contiguous(), group=data_group(pg))
 
     if rank == 0:
         line = {
@@ -674,7 +687,7 @@ def run_cfg3(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_step,
                          "per_launch_ms": ms_local / steps,
                          "timed": "whole decode step (weights + int8 history bytes) per step, CUDA events"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None,
             "e2e": e2e,
             # plan; per layer 2 rmsnorm, qkv_rope_append, attention, swiglu (+ 4 decode-row GEMMs); final rmsnorm
             "gpu_launches": steps * (1 + cfg.layers * 5 + 1),
@@ -731,7 +744,7 @@ def run_encode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         pg.barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
     ranks = per_rank(pg, dev, ms_local, 1, clocks)
-    tt = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    tt = torch.tensor([ms_local], dtype=torch.float64)
     if pg is not None:
         pg.all_reduce(tt, op=pg.ReduceOp.MAX)
     ms_step = float(tt.item())
@@ -755,7 +768,7 @@ def run_encode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "frac": per_step / (ms_local * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
                          "per_launch_bytes": per_call, "per_launch_ms": ms_local / 2,
                          "timed": "two quantize calls (K, V) per step, CUDA events"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0, "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": cpu,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None, "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -802,7 +815,7 @@ def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         pg.barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
     ranks = per_rank(pg, dev, ms_local, 1, clocks)
-    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms_local], dtype=torch.float64)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms_step = float(t.item())
@@ -820,7 +833,7 @@ def run_prefill(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "frac": per_step / (ms_local * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
                          "per_launch_bytes": per_step / 2, "per_launch_ms": ms_local / 2,
                          "timed": "two dequantize calls (K, V) per step, CUDA events"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0, "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": None,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None, "e2e": None, "gpu_launches": 2 * args.steps, "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -877,7 +890,7 @@ def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        t = torch.tensor([x], dtype=torch.float64)
         if pg is not None:
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
@@ -982,7 +995,7 @@ def run_float(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "peak_kind": peak_kind, "per_launch_bytes": per_call, "per_launch_ms": call_ms,
                          "timed": "timed region / attention calls (CUDA events on the launching stream): "
                                   "attn_kernel over float rows, with the plan amortised over the step"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0, "e2e": e2e,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None, "e2e": e2e,
             "gpu_launches": args.steps * (1 + (2 if args.split else 1) * layers),
             "cpu_baseline": cpu,
         }
@@ -1075,7 +1088,7 @@ def run_refmode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        t = torch.tensor([x], dtype=torch.float64)
         if pg is not None:
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
@@ -1195,7 +1208,7 @@ def run_refmode(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "traffic": None, "peak_kind": peak_kind, "per_launch_bytes": per_call,
                          "per_launch_ms": call_us * 1e-3,
                          "timed": "timed region / attention calls (CUDA events), the step's plan charged to its calls"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None,
             "e2e": e2e,
             "gpu_launches": args.steps * (1 + calls),
             "cpu_baseline": cpu,
@@ -1350,7 +1363,7 @@ def run_sample(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
         torch.cuda.synchronize()
     ms_local = start.elapsed_time(end)
     ranks = per_rank(pg, dev, ms_local, args.steps, clocks)
-    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms_local], dtype=torch.float64)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms_step = float(t.item()) / args.steps
@@ -1368,7 +1381,7 @@ def run_sample(args, w, pp, pg, world: int, rank: int, local: int, dev) -> int:
                          "frac": per_call / (us * 1e-6) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
                          "per_launch_bytes": per_call, "per_launch_ms": us * 1e-3,
                          "timed": "64 sampler calls per step in one CUDA graph, CUDA events"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None,
             "e2e": None, "gpu_launches": args.steps * calls, "cpu_baseline": None}), flush=True)
     if pg is not None:
         pg.barrier()
@@ -1500,12 +1513,14 @@ def main() -> int:
     if world > 1:
         import torch.distributed as dist
 
-        # NCCL carries only the final gather and the timing reductions here.  With its default cuMem-backed
-        # buffers (NCCL_CUMEM_ENABLE=1) a CUDA-graph decoder step ran 4.7 % slower on every rank, even with a
-        # one-rank communicator; with plain allocations the step runs as fast as without NCCL.
-        os.environ.setdefault("NCCL_CUMEM_ENABLE", "0")
-
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        # Barriers and the timing reductions go over gloo with host tensors; NCCL carries the outputs' final
+        # gather, over a group created after the timed regions (data_group).  While an NCCL communicator of
+        # two or more ranks exists, a CUDA-graph decoder step (cfg3) runs ~5 % slower on every rank of a B200
+        # box, with or without cuMem buffers and P2P/SHM transports; with only gloo it runs as fast as one
+        # process alone.  All ranks are on this node, so gloo uses the loopback interface.
+        if os.environ.get("MASTER_ADDR", "127.0.0.1") in ("127.0.0.1", "localhost"):
+            os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
         pg = dist
 
     pp = importlib.import_module("pop2-bezier_b200")
@@ -1611,7 +1626,7 @@ def main() -> int:
     barrier()
     ms_total = ms_local = start.elapsed_time(end)
     ranks = per_rank(pg, dev, ms_local, args.steps, clocks)
-    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms_total], dtype=torch.float64)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms_total = float(t.item())
@@ -1668,7 +1683,7 @@ def main() -> int:
         torch.cuda.synchronize()
         barrier()
         def ranks_max(x: float) -> float:
-            te = torch.tensor([x], dtype=torch.float64, device=dev)
+            te = torch.tensor([x], dtype=torch.float64)
             if pg is not None:
                 pg.all_reduce(te, op=pg.ReduceOp.MAX)
             return float(te.item())
@@ -1706,7 +1721,7 @@ def main() -> int:
     if pg is not None:
         # [layers, rows, D] -> per branch [B, layers, H, D], gathered in global branch order on rank 0
         per_branch = outs.view(layers, B, H, D).transpose(0, 1).contiguous()
-        shards.gather(pg, per_branch)
+        shards.gather(pg, per_branch, group=data_group(pg))
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -1726,7 +1741,7 @@ def main() -> int:
                          "per_launch_bytes": per_call, "per_launch_ms": call_ms,
                          "timed": "timed region / attention calls (CUDA events on the launching stream): "
                                   "attn_kernel, with the plan amortised over the step"},
-            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if pg is not None else 0,
+            "clocks": clocks.summary(), "ranks": ranks, "nccl_ranks": world if _DATA_GROUP is not None else 0, "timing_group": "gloo" if pg is not None else None,
             "e2e": e2e,
             # per step: one plan, then per layer the attention kernel (+ the combine kernel with fixed splits)
             "gpu_launches": args.steps * (1 + (2 if args.split else 1) * layers),

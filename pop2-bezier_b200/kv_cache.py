@@ -171,16 +171,17 @@ class BranchShards:
         self.mine = self.members[rank]
         self.widest = max(len(m) for m in self.members)
 
-    def gather(self, dist, out: torch.Tensor) -> torch.Tensor | None:
+    def gather(self, dist, out: torch.Tensor, group=None) -> torch.Tensor | None:
         """`out` is this rank's output, leading dim = len(self.mine) branches.
-        Every rank must call this (it is one collective); rank 0 gets the
-        outputs of all branches in global order, the other ranks get None."""
+        Every rank must call this (it is one collective, over `group`, the
+        default group when None); rank 0 gets the outputs of all branches in
+        global order, the other ranks get None."""
         if out.shape[0] != len(self.mine):
             raise N.PreconditionError(f"gather: {out.shape[0]} branch outputs for a shard of {len(self.mine)}")
         padded = out.new_zeros((self.widest, *out.shape[1:]))
         padded[: len(self.mine)] = out
         parts = [torch.empty_like(padded) for _ in range(self.world)] if self.rank == 0 else None
-        dist.gather(padded, parts, dst=0)
+        dist.gather(padded, parts, dst=0, group=group)
         if self.rank != 0:
             return None
         full = out.new_empty((len(self.shard_of), *out.shape[1:]))

@@ -325,11 +325,14 @@ class BranchScheduler:
             raise errors[0]
         return results
 
-    def run_rank(self, dist, device) -> dict[int, LaneResult] | None:
+    def run_rank(self, dist, device, group=None) -> dict[int, LaneResult] | None:
         """One shard per rank of an initialised process group: this rank runs
-        its LPT shard with no collective until the end, then one gather brings
-        every lane's records (padded to the largest budget) to rank 0, which
-        returns all lanes; the other ranks return None."""
+        its LPT shard with no collective until the end, then one gather (over
+        `group`, the default group when None) brings every lane's records
+        (padded to the largest budget) to rank 0, which returns all lanes; the
+        other ranks return None.  An NCCL communicator that exists while the
+        shards generate slows CUDA-graph steps by ~5 % on B200; a caller that
+        replays graphs creates the NCCL group after generation and passes it."""
         world, rank = dist.get_world_size(), dist.get_rank()
         shards = kv_cache.BranchShards(self.costs, world, rank)
         mine = shards.mine
@@ -341,7 +344,7 @@ class BranchScheduler:
             packed[i, 0, 0] = len(r.records)
             packed[i, 0, 1] = 1 if r.reason == "end" else 0
             packed[i, 1:1 + len(r.records)] = torch.from_numpy(r.records).to(dev)
-        full = shards.gather(dist, packed)
+        full = shards.gather(dist, packed, group=group)
         if full is None:
             return None
         out = {}

@@ -10,6 +10,8 @@ import numpy as np
 import pytest
 import torch
 
+import sched_gpu_setup as G
+
 pytestmark = pytest.mark.gpu
 
 
@@ -31,24 +33,10 @@ def test_device_streams_match_host_and_skip_inactive_rows(pp, cuda):
     assert st.draws.cpu().tolist() == draws
 
 
-def _scheduler(pp, costs, budgets, rows, split):
-    D, sched = pp.decoder, pp.sched
-    cfg = D.DecoderConfig(layers=2, width=256, heads=2, head_dim=128, ffn_hidden=512, max_context=1024)
-    w = sched.default_windows()
-    cap = max(costs) + max(budgets) + 4
-
-    def make_model(shard, lanes, device):
-        return sched.SyntheticPrimitiveModel(cfg, rows, lanes, [costs[ln] for ln in lanes], cap, device, w, seed=5,
-                                             split_tokens=split)
-
-    return sched.BranchScheduler(make_model, costs, 2024, budgets, w)
-
-
 def test_two_shards_match_one_shard_bit_for_bit(pp, cuda):
-    costs = [300, 17, 1000, 64, 512, 5, 700, 128]
-    budgets = [3, 5, 2, 4, 6, 1, 3, 5]
-    one = _scheduler(pp, costs, budgets, rows=8, split=128).run([cuda])
-    two = _scheduler(pp, costs, budgets, rows=8, split=128).run([cuda, cuda])
+    budgets = G.BUDGETS
+    one = G.scheduler(pp).run([cuda])
+    two = G.scheduler(pp).run([cuda, cuda])
     assert sorted(one) == sorted(two) == list(range(8))
     for lane in range(8):
         a, b = one[lane], two[lane]
