@@ -124,6 +124,56 @@ def test_live_against_reference_kernels(pp, cuda, seed):
         np.testing.assert_allclose(host(got), host(want), rtol=0, atol=REF_TOL)
 
 
+REF_CUBIN = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                         "int8_kv_ref.cubin")
+
+
+@pytest.mark.parametrize("lengths", ["uniform", "ragged"])
+def test_deployed_shape_every_row(pp, oracle, cuda, lengths):
+    """The reference model's own step shape: 8 branches x 24 heads, d 64,
+    capacity 1024, reference mode.  With every branch at 1023 history tokens
+    the plan gives each CTA whole rows; with ragged histories it cuts rows
+    across CTAs.  Every row of three layer calls on one plan (the later two
+    streaming history before the previous call ends) is checked against the
+    oracle and, where the reference's kernels were built, against them."""
+    ops = pp.int8_kv_ops
+    g = np.random.Generator(np.random.PCG64(64 + (lengths == "ragged")))
+    branches, heads, cap, d = 8, 24, 1024, 64
+    rows = branches * heads
+    if lengths == "uniform":
+        past_h = np.full(branches, cap - 1, dtype=np.int32)
+    else:
+        past_h = g.integers(0, cap, branches).astype(np.int32)
+        past_h[0], past_h[1] = 0, cap - 1
+    past = torch.tensor(past_h, device=cuda)
+    layers = []
+    for _ in range(3):
+        k, ks = ops.quantize(to_dev(g.standard_normal((rows, cap, d), dtype=np.float32), cuda))
+        v, vs = ops.quantize(to_dev(g.standard_normal((rows, cap, d), dtype=np.float32), cuda))
+        q, sk, sv = (to_dev(g.standard_normal((rows, d), dtype=np.float32), cuda) for _ in range(3))
+        layers.append((q, k, v, ks, vs, sk, sv))
+    k0, v0, ks0, vs0 = layers[0][1:5]
+    params = ops.attn_params(q_dtype=torch.float32, out_dtype=torch.float32)
+    ws = ops.new_workspace(ops.arena_struct(k0, v0, ks0, vs0, heads), params, cuda)
+    ops.plan_ragged(k0, v0, ks0, vs0, past, heads, ws, scratch=True)
+    outs = [ops.decode_attention(q, k, v, ks, vs, past, heads, scratch_k=sk, scratch_v=sv, out_dtype=torch.float32,
+                                 workspace=ws, plan_ready=True, prefetch_history=i > 0)
+            for i, (q, k, v, ks, vs, sk, sv) in enumerate(layers)]
+    ref = None
+    if os.path.exists(REF_CUBIN):
+        from ref_runner import RefInt8Kernels
+
+        ref = RefInt8Kernels()
+    for (q, k, v, ks, vs, sk, sv), out in zip(layers, outs):
+        want = oracle.attention(host(q), k.cpu().numpy(), v.cpu().numpy(), ks.cpu().numpy(), vs.cpu().numpy(),
+                                past_h, heads, sk=host(sk), sv=host(sv), threads=oracle.max_threads())
+        np.testing.assert_allclose(host(out), want.reshape(rows, d), rtol=0, atol=REF_TOL)
+        if ref is not None:
+            r = ref.attention(q.view(rows, 1, d), k, v, ks, vs, sk.view(rows, 1, d), sv.view(rows, 1, d), past, heads,
+                              128)
+            np.testing.assert_allclose(host(out), host(r).reshape(rows, d), rtol=0, atol=REF_TOL)
+
+
 def assert_bf16_close(got, ref_f32):
     """bf16 outputs: the f32 result must round to within one bf16 ulp of the
     oracle's f32 result rounded the same way (output rounding is up to 2^-8
