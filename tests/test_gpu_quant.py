@@ -3,6 +3,8 @@ bit-exact against the oracle and against the reference kernels' own codes
 (tests/golden/ref_int8kv.npz)."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -94,6 +96,33 @@ def test_quantize_near_ties_bit_exact(pp, oracle, cuda, d, dtype):
     assert np.array_equal(arena.k[:, 2].cpu().numpy(), ref_codes)
     assert np.array_equal(arena.v[:, 2].cpu().numpy(), ref_codes)
     assert np.array_equal(u32(arena.k_scale[:, 2].cpu().numpy()), u32(ref_scales))
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                                    "oracle", "_ref", "int8_kv_ref.cubin")),
+                    reason="reference kernels were not built (no reference tree when this checkout was built)")
+def test_quantize_large_arena_live_against_reference_kernels(pp, cuda):
+    """A cfg1-sized arena at the reference's head size (512 rows x 4096 tokens
+    x 64, heavy-tailed values, every 7th token built on or next to half-integer
+    quotients): codes and scales from pp_i8_scale + pp_i8_pack and from this
+    library, byte for byte."""
+    from ref_runner import RefInt8Kernels
+
+    ref = RefInt8Kernels()
+    g = torch.Generator(device=cuda)
+    g.manual_seed(97)
+    x = torch.randn(512, 4096, 64, device=cuda, generator=g)
+    x = x * torch.exp(torch.randn(512, 4096, 1, device=cuda, generator=g))  # per-token magnitude spread
+    # every 7th token: half-integer multiples of amax / 127 (quotients x / s on or next to ties)
+    amax = x[:, ::7].abs().amax(-1, keepdim=True)
+    ties = torch.randint(-254, 255, x[:, ::7].shape, device=cuda, generator=g).float() * 0.5
+    ties[..., 0] = 127.0
+    x[:, ::7] = ties * (amax / 127.0)
+    want_codes, want_scales = ref.quantize(x.contiguous())
+    codes, scales = pp.int8_kv_ops.quantize(x.contiguous())
+    assert torch.equal(codes, want_codes)
+    assert torch.equal(scales.view(torch.int32), want_scales.view(torch.int32))
+    del x, ties
 
 
 def test_quantize_matches_reference_kernel_codes(pp, cuda, golden):

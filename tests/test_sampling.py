@@ -63,6 +63,39 @@ def test_sampler_bit_exact_with_reference_kernel(pp, cuda, renyi_golden, case):
 
 
 @pytest.mark.gpu
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                                    "oracle", "_ref", "renyi_ref.cubin")),
+                    reason="the reference sampler was not built (no reference tree when this checkout was built)")
+@pytest.mark.parametrize("ties", [False, True])
+def test_sampler_random_heads_live_against_reference_kernel(pp, cuda, ties):
+    """Random heads through the reference's own kernel and ours in one process,
+    bit for bit on every row (both use the same fast exp/log).  With `ties`
+    the logits sit on a coarse grid with +0 and -0 among them, so the rank-th
+    token is often one of many equal values and the column order decides."""
+    from ref_runner import RefRenyiKernel
+
+    ref = RefRenyiKernel()
+    g = np.random.Generator(np.random.PCG64(71 + ties))
+    for batch, choices, guidance, alpha, cfg in ((64, 2048, 2, 4.0, 1.5), (96, 1000, 1, 2.0, 1.0),
+                                                 (40, 257, 2, 8.0, 3.0), (33, 2048, 1, 1.5, 1.0)):
+        raw = (g.standard_normal((batch * guidance, choices)) * g.uniform(0.1, 6.0)).astype(np.float32)
+        if ties:
+            raw = np.round(raw * 2.0) / 2.0
+            raw[np.abs(raw) == 0] = np.where(g.uniform(size=(raw == 0).sum()) < 0.5, -0.0, 0.0)
+            raw = raw.astype(np.float32)
+        u = g.uniform(0, 1, batch).astype(np.float32)
+        u[:3] = np.array([0.0, np.nextafter(np.float32(1), np.float32(0)), 0.5], np.float32)
+        starts = g.integers(0, choices // 2, batch)
+        bounds = np.stack([starts, g.integers(1, choices - starts + 1)], 1).astype(np.uint32)
+        raw_d, u_d = torch.from_numpy(raw).to(cuda), torch.from_numpy(u).to(cuda)
+        b_d = torch.from_numpy(bounds.astype(np.int32)).to(cuda)
+        tok, ok, sup = pp.sampling.renyi_sample(raw_d, u_d, b_d, alpha, cfg, guidance, 11)
+        got = torch.stack([tok.view(-1), ok.view(-1), sup.view(-1)]).cpu().numpy().view(np.uint32)
+        want = ref.sample(raw_d, u_d, b_d, guidance, alpha, cfg, 11).cpu().numpy().view(np.uint32)
+        np.testing.assert_array_equal(got, want, err_msg=f"{batch}x{choices} guidance {guidance}")
+
+
+@pytest.mark.gpu
 def test_sampler_random_heads_vs_oracle(pp, oracle, cuda):
     """Larger random batches: every row's (token, flag, support) as the oracle's."""
     g = np.random.Generator(np.random.PCG64(61))
