@@ -425,7 +425,8 @@ int32_t pp_b200_decode_attention(const PpKvArena* arena, const PpAttnParams* par
     L.q = q;
     L.out = out;
     L.status = status;
-    const uint32_t stage = pp::attention_stage_tokens(arena->head_dim);  // rows of one whole-stage box
+    L.short_stages = pp::attention_short_stages(arena->head_dim, arena->rows, arena->capacity, L.max_ctas);
+    const uint32_t stage = pp::attention_stage_tokens(arena->head_dim, L.short_stages);  // rows of one whole-stage box
     for (int i = 0; i < pp::kTailBoxes; ++i) {
         if ((s = encode_codes_map(&L.tails.k[i], arena->k, *arena, 16u << i))) return s;
         if ((s = encode_codes_map(&L.tails.v[i], arena->v, *arena, 16u << i))) return s;

@@ -117,6 +117,7 @@ struct AttnLaunch {
     bool plan_ready;
     bool prefetch;  // PP_ATTN_PREFETCH_HISTORY
     bool use_pdl;
+    bool short_stages;  // int8 head_dim 64 with few tokens per CTA: the 12-warp, 384-token-stage kernel
     // Tensor maps (host-encoded): K, V codes in whole-stage boxes and in the
     // tail boxes, and K, V scales (int8 only).  Float K/V maps are 3-D
     // {channel, token, row} with one 128-byte panel per box.
@@ -161,7 +162,8 @@ cudaError_t launch_attention(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t launch_combine(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t configure_attention_kernels(int device);
 uint32_t attention_scale_box_elems();
-uint32_t attention_stage_tokens(uint32_t head_dim);
+bool attention_short_stages(uint32_t head_dim, uint32_t rows, uint32_t capacity, uint32_t ctas);
+uint32_t attention_stage_tokens(uint32_t head_dim, bool short_stages);
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind);
 cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t stream);
 cudaError_t launch_lane_uniforms(const uint64_t* seeds, uint64_t* draws, const uint32_t* active, uint32_t rows,

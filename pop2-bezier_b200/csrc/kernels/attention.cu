@@ -437,12 +437,21 @@ struct RegPartial {
 #ifndef PP_ATTN_STAGES_D64
 #define PP_ATTN_STAGES_D64 3  // 480-token stages of 64 KB: three fit
 #endif
+// int8 head_dim 64 calls with few tokens per CTA (the reference model's own
+// steps: rows of at most 1024 tokens) run 12 consumer warps, 384-token stages:
+// the ring fills and drains sooner, and a 1023-token row is three stages
+#ifndef PP_ATTN_NC_SHORT_D64
+#define PP_ATTN_NC_SHORT_D64 12
+#endif
+#ifndef PP_ATTN_SHORT_TOKENS_PER_CTA
+#define PP_ATTN_SHORT_TOKENS_PER_CTA 6144  // rows x capacity per CTA at most this: short stages
+#endif
 
 // Element type of the K/V history: int8 codes with per-token scales (the
 // int8 arena), or plain bf16 / f32 rows (the float-KV cache).
 enum class Kv : int { I8 = kKvInt8, BF16 = kKvBf16, F32 = kKvF32 };
 
-template <int D, Kv KV = Kv::I8>
+template <int D, Kv KV = Kv::I8, int NCW = 0>  // NCW: consumer warps (0: by row width)
 struct Cfg {
     static constexpr bool SCALED = KV == Kv::I8;    // int8 codes + scale arrays
     static constexpr int ELEM = KV == Kv::I8 ? 1 : KV == Kv::BF16 ? 2 : 4;
@@ -454,7 +463,7 @@ struct Cfg {
     static constexpr int PANELS = ROW / PANEL;
     // consumer warps: all 15 while a stage of 240 tokens fits ~62 KB, fewer
     // (fewer tokens per stage) for the wider float rows
-    static constexpr int NC = ROW <= 128 ? PP_ATTN_NC : ROW == 256 ? 8 : 4;
+    static constexpr int NC = NCW ? NCW : ROW <= 128 ? PP_ATTN_NC : ROW == 256 ? 8 : 4;
     static constexpr int THREADS = (NC + 1) * 32;   // + one producer warp
     static constexpr int BOX = 16;                  // tokens per MMA block and per tail TMA box
     // MMA blocks per consumer warp per stage (independent blocks interleaved for ILP)
@@ -600,13 +609,13 @@ __device__ __forceinline__ uint32_t u4_word(const uint4& v, int w) {
     return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
 }
 
-template <int D, typename QT, Kv KV>
-__global__ void __launch_bounds__(Cfg<D, KV>::THREADS, 1)
+template <int D, typename QT, Kv KV, int NCW>
+__global__ void __launch_bounds__(Cfg<D, KV, NCW>::THREADS, 1)
     attn_kernel(const __grid_constant__ TailMaps tails,
                 const __grid_constant__ CUtensorMap map_k_stage, const __grid_constant__ CUtensorMap map_v_stage,
                 const __grid_constant__ CUtensorMap map_ks, const __grid_constant__ CUtensorMap map_vs,
                 const AttnArgs args) {
-    using C = Cfg<D, KV>;
+    using C = Cfg<D, KV, NCW>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -1358,9 +1367,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
                       load_scratch<D, QT>(lane, r, a.q, a.sk, a.sv, a.scale_log2), a.out);
 }
 
-template <int D, typename QT, Kv KV>
+template <int D, typename QT, Kv KV, int NCW = 0>
 cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
-    using C = Cfg<D, KV>;
+    using C = Cfg<D, KV, NCW>;
     AttnArgs args{};
     args.q = L.q;
     args.q_stride = L.q_stride;
@@ -1388,7 +1397,7 @@ cudaError_t launch_attn_t(const AttnLaunch& L, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = L.use_pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT, KV>, L.tails, L.map_k_stage, L.map_v_stage, L.map_ks,
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, QT, KV, NCW>, L.tails, L.map_k_stage, L.map_v_stage, L.map_ks,
                               L.map_vs, args);
 }
 
@@ -1439,10 +1448,10 @@ cudaError_t launch_wait_probe(uint32_t* status, uint64_t limit_ns, cudaStream_t 
 }
 
 namespace {
-template <int D, typename QT, Kv KV>
+template <int D, typename QT, Kv KV, int NCW = 0>
 cudaError_t configure_one() {
-    return cudaFuncSetAttribute(attn_kernel<D, QT, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                Cfg<D, KV>::SMEM_BYTES);
+    return cudaFuncSetAttribute(attn_kernel<D, QT, KV, NCW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Cfg<D, KV, NCW>::SMEM_BYTES);
 }
 template <Kv KV>
 cudaError_t configure_kind() {
@@ -1450,13 +1459,23 @@ cudaError_t configure_kind() {
     if ((e = configure_one<128, float, KV>()) != cudaSuccess) return e;
     if ((e = configure_one<128, __nv_bfloat16, KV>()) != cudaSuccess) return e;
     if ((e = configure_one<64, float, KV>()) != cudaSuccess) return e;
-    return configure_one<64, __nv_bfloat16, KV>();
+    if ((e = configure_one<64, __nv_bfloat16, KV>()) != cudaSuccess) return e;
+    if constexpr (KV == Kv::I8) {
+        if ((e = configure_one<64, float, KV, PP_ATTN_NC_SHORT_D64>()) != cudaSuccess) return e;
+        if ((e = configure_one<64, __nv_bfloat16, KV, PP_ATTN_NC_SHORT_D64>()) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 template <Kv KV>
 cudaError_t launch_kind(const AttnLaunch& L, cudaStream_t stream) {
     const bool bq = L.q_dtype == PP_DTYPE_BF16;
     if (L.arena.head_dim == 128)
         return bq ? launch_attn_t<128, __nv_bfloat16, KV>(L, stream) : launch_attn_t<128, float, KV>(L, stream);
+    if constexpr (KV == Kv::I8) {
+        if (L.short_stages)
+            return bq ? launch_attn_t<64, __nv_bfloat16, KV, PP_ATTN_NC_SHORT_D64>(L, stream)
+                      : launch_attn_t<64, float, KV, PP_ATTN_NC_SHORT_D64>(L, stream);
+    }
     return bq ? launch_attn_t<64, __nv_bfloat16, KV>(L, stream) : launch_attn_t<64, float, KV>(L, stream);
 }
 }  // namespace
@@ -1469,7 +1488,14 @@ cudaError_t configure_attention_kernels(int /*device*/) {
 }
 
 uint32_t attention_scale_box_elems() { return Cfg<128>::SC_BOX; }
-uint32_t attention_stage_tokens(uint32_t head_dim) { return head_dim == 128 ? Cfg<128>::STAGE_BOX : Cfg<64>::STAGE_BOX; }
+bool attention_short_stages(uint32_t head_dim, uint32_t rows, uint32_t capacity, uint32_t ctas) {
+    return head_dim == 64 && ctas &&
+           (uint64_t)rows * capacity <= (uint64_t)PP_ATTN_SHORT_TOKENS_PER_CTA * ctas;
+}
+uint32_t attention_stage_tokens(uint32_t head_dim, bool short_stages) {
+    if (head_dim == 128) return Cfg<128>::STAGE_BOX;
+    return short_stages ? Cfg<64, Kv::I8, PP_ATTN_NC_SHORT_D64>::STAGE_BOX : Cfg<64>::STAGE_BOX;
+}
 uint32_t attention_float_stage_tokens(uint32_t head_dim, int kv_kind) {
     if (kv_kind == kKvBf16) return head_dim == 128 ? Cfg<128, Kv::BF16>::T : Cfg<64, Kv::BF16>::T;
     return head_dim == 128 ? Cfg<128, Kv::F32>::T : Cfg<64, Kv::F32>::T;

@@ -210,6 +210,30 @@ def _random_arena(pp, branches, heads, d, cap, dev, seed, dist="normal"):
     return k, v, ks, vs, g
 
 
+@pytest.mark.parametrize("max_ctas", [0, 8])
+@pytest.mark.parametrize("scratch", [False, True])
+def test_head_dim_64_both_stage_configs(pp, oracle, cuda, max_ctas, scratch):
+    """int8 head_dim 64 runs the 12-warp, 384-token-stage kernel when the
+    arena holds at most 6144 tokens per CTA and the 15-warp, 480-token one
+    above that: 64 rows x 2048 tokens on all SMs takes the first, on 8 CTAs
+    the second.  Every row against the oracle, history and reference mode."""
+    ops = pp.int8_kv_ops
+    branches, heads, cap, d = 16, 4, 2048, 64
+    k, v, ks, vs, g = _random_arena(pp, branches, heads, d, cap, cuda, 640 + max_ctas + scratch)
+    rows = branches * heads
+    lens_h = [cap, 1, 2047, 1023, 480, 481, 17, 0 if scratch else 5, 1500, 961, 384, 385, 2000, 33, 767, 1152]
+    lens = torch.tensor(lens_h, dtype=torch.int32, device=cuda)
+    q = torch.randn(rows, d, device=cuda, generator=g)
+    sk = torch.randn(rows, d, device=cuda, generator=g) if scratch else None
+    sv = torch.randn(rows, d, device=cuda, generator=g) if scratch else None
+    if scratch:
+        lens = torch.clamp(lens, max=cap - 1)  # reference mode: history plus the scratch token
+    out = ops.decode_attention(q, k, v, ks, vs, lens, heads, scratch_k=sk, scratch_v=sv, out_dtype=torch.float32,
+                               max_ctas=max_ctas)
+    ref = _oracle_all(oracle, q, k, v, ks, vs, lens.cpu().numpy(), heads, sk=sk, sv=sv)
+    np.testing.assert_allclose(host(out), ref, rtol=1e-5, atol=2e-5)
+
+
 def _oracle_rows(oracle, q, k, v, ks, vs, lens, heads, pick, sk=None, sv=None):
     idx = torch.as_tensor(pick, device=k.device)
     sub = lambda t: t[idx].cpu().numpy()  # noqa: E731
