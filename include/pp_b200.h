@@ -78,7 +78,10 @@ typedef struct PpKvArena {
 /* Attention options. */
 typedef struct PpAttnParams {
     uint32_t struct_size;   /* sizeof(PpAttnParams) */
-    uint32_t split_tokens;  /* 0: automatic stream-K balance over all SMs;
+    uint32_t split_tokens;  /* 0: automatic: equal tokens per SM (stream-K), or
+                               whole rows per CTA when the rows are of one
+                               length and that costs little more; split rows
+                               are merged inside the attention kernel;
                                else: fixed split size in tokens (the reference's
                                split_tokens, int8_kv_ops.rs:52) */
     int32_t q_dtype;        /* PP_DTYPE_F32 or PP_DTYPE_BF16, q is [rows, head_dim] */
