@@ -210,6 +210,38 @@ def _random_arena(pp, branches, heads, d, cap, dev, seed, dist="normal"):
     return k, v, ks, vs, g
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("scratch", [False, True])
+def test_batched_branches_match_single_branch_calls(pp, cuda, d, scratch):
+    """The reference checks its batched forward against one sequence at a time
+    (app/src/model/batch.rs:389-475).  Here: one call over a ragged batch of
+    branches against one call per branch on that branch's rows of the same
+    arena.  With fixed splits every row is computed and merged alone, so the
+    two agree bit for bit; the automatic plan cuts rows differently in the
+    two cases, so they agree to f32 rounding."""
+    ops = pp.int8_kv_ops
+    branches, heads, cap = 6, 4, 900
+    k, v, ks, vs, g = _random_arena(pp, branches, heads, d, cap, cuda, 4000 + d + scratch)
+    rows = branches * heads
+    lens_h = [899, 1, 513, 0 if scratch else 7, 256, 640]
+    lens = torch.tensor(lens_h, dtype=torch.int32, device=cuda)
+    q = torch.randn(rows, d, device=cuda, generator=g)
+    sk = torch.randn(rows, d, device=cuda, generator=g) if scratch else None
+    sv = torch.randn(rows, d, device=cuda, generator=g) if scratch else None
+    for split in (128, 0):
+        batched = ops.decode_attention(q, k, v, ks, vs, lens, heads, scratch_k=sk, scratch_v=sv,
+                                       out_dtype=torch.float32, split_tokens=split)
+        for b in range(branches):
+            rs = slice(b * heads, (b + 1) * heads)
+            one = ops.decode_attention(q[rs], k[rs], v[rs], ks[rs], vs[rs], lens[b:b + 1], heads,
+                                       scratch_k=None if sk is None else sk[rs], scratch_v=None if sv is None else sv[rs],
+                                       out_dtype=torch.float32, split_tokens=split)
+            if split:
+                assert torch.equal(one, batched[rs]), f"branch {b}"
+            else:
+                np.testing.assert_allclose(host(one), host(batched[rs]), rtol=1e-5, atol=2e-6, err_msg=f"branch {b}")
+
+
 @pytest.mark.parametrize("max_ctas", [0, 8])
 @pytest.mark.parametrize("scratch", [False, True])
 def test_head_dim_64_both_stage_configs(pp, oracle, cuda, max_ctas, scratch):
